@@ -1,0 +1,53 @@
+"""Build the CUDA library in-tree for sm_100a.
+
+    python -m atomflow_b200.build          # -> atomflow_b200/libatomflow_b200.so
+
+nvcc cross-compiles without a GPU, so this runs on any machine with CUDA 12.8+.
+The shared CUDA runtime is linked so the library shares the process's current
+device and streams with any other CUDA user in the process (e.g. PyTorch).
+"""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIB = PKG / "libatomflow_b200.so"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-cudart", "shared"]
+
+
+def sources():
+    return sorted(CSRC.glob("*.cu"))
+
+
+def headers():
+    return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
+
+
+def up_to_date() -> bool:
+    if not LIB.exists():
+        return False
+    t = LIB.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in sources() + headers())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and up_to_date():
+        return LIB
+    nvcc = os.environ.get("NVCC", "nvcc")
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [nvcc, *ARCH, *FLAGS, "-shared", "-I", str(ROOT / "include"), "-o", str(tmp),
+           *map(str, sources())]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True, cwd=str(PKG))
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    print(LIB)

@@ -1,0 +1,95 @@
+// af_common.cuh -- device helpers shared by the sm_100a kernels of this library.
+//
+// Inline PTX only for what the CUDA C++ surface does not expose directly:
+// streaming loads that skip L1, L2-only loads for data another kernel wrote,
+// the packed FP8x2 -> FP16x2 conversion, the m16n8k16 tensor-core MMA and the
+// programmatic-dependent-launch controls.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "../../include/atomflow_b200.h"
+
+namespace af {
+
+// Weight streams are read exactly once per call: keep them out of L1 so the
+// activations and scales that are re-read stay resident there.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// L2-coherent load for data produced by an earlier kernel of the stream
+// (activations) or by another CTA of this grid (split-K partials).
+__device__ __forceinline__ uint4 ldcg_u4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float4 ldcg_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ldcg_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int ldcg_s32(const int* p) {
+    int v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// Two E4M3 bytes (low 16 bits / high 16 bits of a word) -> one f16x2 register.
+// The byte at the lower address lands in the lower half.  E4M3 -> FP16 is exact.
+__device__ __forceinline__ uint32_t e4m3x2_lo(uint32_t w) {
+    uint32_t r;
+    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %1; cvt.rn.f16x2.e4m3x2 %0, lo; }" : "=r"(r) : "r"(w));
+    return r;
+}
+__device__ __forceinline__ uint32_t e4m3x2_hi(uint32_t w) {
+    uint32_t r;
+    asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %1; cvt.rn.f16x2.e4m3x2 %0, hi; }" : "=r"(r) : "r"(w));
+    return r;
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, FP32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Programmatic dependent launch: let the next kernel of the stream start its
+// independent prologue (weight prefetch) now, and block until the previous
+// kernel's memory is visible before touching anything it may have written.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+
+// Lowest index wins ties; NaN never wins; idx < 0 means "no candidate".
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+    if (i < 0 || v != v) return false;
+    if (bi < 0) return true;
+    return v > bv || (v == bv && i < bi);
+}
+
+}  // namespace af

@@ -1,0 +1,46 @@
+// af_internal.h -- host-side plumbing shared by the launchers (not installed).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/atomflow_b200.h"
+
+namespace af {
+
+constexpr int kMaxDevices = 64;
+
+// Streaming multiprocessors of the current device (cached per device).
+int device_sm_count(int* device_out = nullptr);
+
+// Record a CUDA failure for af_last_cuda_error() and map it to AF_ERR_CUDA.
+af_status cuda_fail(cudaError_t e, const char* where);
+
+// CTAs launched per SM by the streaming kernels (default 1; AF_CTAS_PER_SM
+// overrides it for tuning experiments).
+int ctas_per_sm();
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Launch `kernel` with programmatic stream serialization, so it may begin
+// while the previous kernel of the stream drains; the kernel itself calls
+// griddepcontrol.wait before touching data that kernel may have written.
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+}  // namespace af

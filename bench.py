@@ -1,0 +1,438 @@
+"""Benchmark of the W8A16 decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload layerset|gemv:N:K[:M]|lmhead:f16|lmhead:fp8]
+
+Default workload: the Llama-3.2-3B-shaped projection set
+at M = 1 -- fused QKV [5120x3072], O [3072x3072], gate and up [8192x3072],
+down [3072x8192] -- for 28 independent layers (2.82 GB of FP8 weights plus
+FP16 group scales, far larger than the 126 MB L2, so no flush is needed).
+One step = the 140 GEMVs in layer order, one CUDA-graph replay.  The metric is
+achieved HBM GB/s over the algorithmic bytes (W + scales + x + y).
+
+Arms
+  ours       this library through its C ABI (af_w8a16_gemv), graph-captured.
+  reference  the reference's own w8a16_gemv_kernel (src/kernel/qkv_gemm.cu,
+             compiled from its sources into oracle/_ref/libafref.so) on the
+             same data, graph-captured like the reference's main.cu.  The
+             reference's path is CUDA, so this arm runs on the GPU.
+
+N > 1 ranks (torchrun): Megatron tensor parallelism of the same layer set --
+QKV/gate/up column-split, O/down row-split followed by an NCCL all-reduce of
+the partial outputs.  Total work is fixed (strong scaling); `value` counts the
+bytes all ranks stream divided by the slowest rank's time.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from atomflow_b200 import lib as af_lib  # noqa: E402
+from atomflow_b200.quant import quantize_gs128, quantize_row  # noqa: E402
+
+D, FFN, QKV = 3072, 8192, 5120
+NLAYERS = 28
+PROJ = [("qkv", QKV, D, "col"), ("o", D, D, "row"), ("gate", FFN, D, "col"),
+        ("up", FFN, D, "col"), ("down", D, FFN, "row")]
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ------------------------------------------------------------------ utils
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.samples = []
+        self.proc = None
+        self.ok = True
+        try:
+            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            ident = ["--id=" + bus] if bus else []
+        except Exception:
+            ident = []
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                                          "-lms", "200", *ident], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.ok = False
+            return
+        self.marks = []
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [c.strip() for c in line.split(",")]))
+
+    def mark(self):
+        return time.time()
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [r for (t, r) in self.samples if t0 - 0.25 <= t <= t1 + 0.25] or [r for _, r in self.samples]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "power_w_max": max(pw) if pw else None, "samples": len(rows)}
+
+
+def algorithmic_bytes(N, K, M=1, scale="group"):
+    sb = N * (K // 128) * 2 if scale == "group" else (N * 4 if scale == "row" else 0)
+    return N * K + sb + M * K * 2 + M * N * 2
+
+
+# --------------------------------------------------------------- workload
+
+def make_layerset(device, rank, world, seed=1234):
+    """Config-1 weights: per (layer, projection) W ~ N(0, 0.02) quantised to E4M3
+    with FP16 group scales (the reference's format); x ~ N(0, 1) FP16.  Under TP
+    each rank keeps its shard of every projection."""
+    items = []
+    g = torch.Generator(device=device)
+    for layer in range(NLAYERS):
+        for pi, (name, N, K, split) in enumerate(PROJ):
+            g.manual_seed(seed + 1000 * layer + pi)
+            w = torch.randn(N, K, generator=g, device=device, dtype=torch.float32) * 0.02
+            x = torch.randn(1, K, generator=g, device=device, dtype=torch.float32).half()
+            if world > 1 and split == "col":
+                w = w.chunk(world, 0)[rank]
+            elif world > 1:
+                w = w.chunk(world, 1)[rank]
+                x = x.chunk(world, 1)[rank]
+            q, s = quantize_gs128(w.contiguous())
+            del w
+            items.append(dict(name=name, layer=layer, N=q.shape[0], K=q.shape[1], split=split,
+                              q=q.view(torch.uint8).contiguous(), s=s.contiguous(), x=x.contiguous(),
+                              y=torch.zeros(1, q.shape[0], dtype=torch.float16, device=device)))
+    return items
+
+
+def make_single(device, N, K, M, seed=99):
+    """One GEMV shape, with enough rotating weight copies to exceed 4x L2."""
+    copies = max(2, int(np.ceil(4 * 128e6 / (N * K))))
+    items = []
+    g = torch.Generator(device=device)
+    for i in range(copies):
+        g.manual_seed(seed + i)
+        w = torch.randn(N, K, generator=g, device=device) * 0.02
+        q, s = quantize_gs128(w)
+        x = torch.randn(M, K, generator=g, device=device).half()
+        items.append(dict(name=f"gemv{i}", layer=i, N=N, K=K, split="col", q=q.view(torch.uint8), s=s, x=x,
+                          y=torch.zeros(M, N, dtype=torch.float16, device=device)))
+    return items
+
+
+# ------------------------------------------------------------------- arms
+
+class OursGemv:
+    def __init__(self, items, device):
+        self.L = af_lib()
+        self.items = items
+        need = max(self.L.af_w8a16_gemv_workspace_bytes(it["x"].shape[0], it["N"], it["K"], 0) for it in items)
+        self.ws = torch.zeros(need, dtype=torch.uint8, device=device)
+
+    def launch(self, stream, it, xptr=None, yptr=None):
+        rc = self.L.af_w8a16_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
+                                  yptr or it["y"].data_ptr(), it["x"].shape[0], it["N"], it["K"], 128, 0,
+                                  self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"af_w8a16_gemv: {self.L.af_status_string(rc).decode()}")
+
+
+class RefGemv:
+    def __init__(self, items, device):
+        sys.path.insert(0, str(ROOT))
+        import oracle
+        self.L = oracle.ref()
+        if self.L is None:
+            raise FileNotFoundError("oracle/_ref/libafref.so")
+        self.items = items
+
+    def launch(self, stream, it, xptr=None, yptr=None):
+        rc = self.L.afref_w8a16_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
+                                     yptr or it["y"].data_ptr(), it["N"], it["K"], stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"reference launch failed ({rc})")
+
+
+def capture_step(arm, items, stream, allreduce=None, pre=None, post=None):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        # one eager pass (sets kernel attributes, NCCL warm-up) before capture
+        if pre:
+            pre()
+        for it in items:
+            arm.launch(stream, it)
+            if allreduce is not None and it["split"] == "row":
+                allreduce(it["y"])
+        if post:
+            post()
+    stream.synchronize()
+    with torch.cuda.graph(g, stream=stream):
+        if pre:
+            pre()
+        for it in items:
+            arm.launch(stream, it)
+            if allreduce is not None and it["split"] == "row":
+                allreduce(it["y"])
+        if post:
+            post()
+    return g
+
+
+def time_graph(g, stream, steps, warmup, dist_on):
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    ms = ev0.elapsed_time(ev1)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms, t0, t1
+
+
+# ------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(items, budget_s=10.0):
+    """The reference's GEMV arithmetic as a host loop (oracle, OpenMP over rows,
+    bit-identical to the reference kernel) on a bounded sample of the workload:
+    the first layer's five projections, repeated until ~budget_s have passed."""
+    import oracle
+    L = oracle.cpu()
+    L.af_oracle_gemv_cpu_baseline.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 2 + [ctypes.c_void_p, ctypes.c_int]
+    sample = items[:5]
+    host = [(it["x"].cpu().numpy().view(np.uint16).copy(), it["q"].cpu().numpy().copy(),
+             it["s"].cpu().numpy().view(np.uint16).copy(), np.empty(it["N"], np.uint16), it["N"], it["K"])
+            for it in sample]
+    cores = os.cpu_count() or 1
+    nbytes = sum(algorithmic_bytes(N, K) for (_, _, _, _, N, K) in host)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for x, q, s, y, N, K in host:
+            L.af_oracle_gemv_cpu_baseline(x.ctypes.data, q.ctypes.data, s.ctypes.data, N, K, y.ctypes.data, cores)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes * reps / dt / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"layer 0's 5 projections (M=1, {nbytes / 1e6:.1f} MB algorithmic) x {reps} passes, "
+                      f"{dt:.1f} s, {cores} OpenMP threads"}
+
+
+# -------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="layerset")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    if args.impl == "reference" and dist_on and rank != 0:
+        return 0                     # the reference arm runs on rank 0 alone
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if dist_on and args.impl == "ours":
+        torch.distributed.init_process_group("nccl", device_id=device)
+    tp = world if (dist_on and args.impl == "ours") else 1
+    trank = rank if tp > 1 else 0
+
+    wl = args.workload
+    if wl == "layerset":
+        items = make_layerset(device, trank, tp)
+        config = {"workload": "llama3.2-3b layer-set x28 (BASELINE config 1)", "M": 1,
+                  "shapes": "qkv 5120x3072, o 3072x3072, gate/up 8192x3072, down 3072x8192",
+                  "scales": "fp16 per 128-group (reference format)", "gemvs_per_step": len(items),
+                  "weights_gb": round(sum(it["q"].numel() for it in items) * tp / 1e9, 3),
+                  "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
+                  "parallelism": f"tp{tp}" if tp > 1 else "single"}
+    elif wl.startswith("gemv:"):
+        parts = [int(v) for v in wl.split(":")[1:]]
+        N, K = parts[0], parts[1]
+        M = parts[2] if len(parts) > 2 else 1
+        items = make_single(device, N, K, M)
+        config = {"workload": f"single GEMV {N}x{K} M={M}", "M": M, "copies": len(items),
+                  "l2": f"{len(items)} rotating weight copies ({len(items) * N * K / 1e6:.0f} MB) > 4x L2",
+                  "parallelism": "single"}
+    else:
+        raise SystemExit(f"unknown workload {wl}")
+
+    arm = OursGemv(items, device) if args.impl == "ours" else None
+    if args.impl == "reference":
+        try:
+            arm = RefGemv(items, device)
+        except FileNotFoundError as e:
+            print(json.dumps({"impl": "reference", "unavailable": f"{e} not built (needs the reference sources)"}))
+            return 0
+    stream = torch.cuda.Stream(device)
+    allreduce = None
+    if tp > 1:
+        def allreduce(y):
+            torch.distributed.all_reduce(y)
+
+    step_bytes = sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items)
+    total_bytes = step_bytes * tp
+    g = capture_step(arm, items, stream, allreduce)
+    sampler = ClockSampler(local) if rank == 0 else None
+    ms, t0, t1 = time_graph(g, stream, args.steps, args.warmup, dist_on)
+    clocks = sampler.summary(t0, t1) if sampler else None
+    ms_step = ms / args.steps
+    value = total_bytes / (ms_step / 1e3) / 1e9
+    launches = len(items) * args.steps
+
+    e2e = None
+    if not args.no_e2e:
+        # End to end through the C ABI with host buffers: every step copies all
+        # 140 activation vectors from pinned host memory, runs the GEMVs and
+        # copies every output back; graph-captured like the reference's decode.
+        xs_host = torch.cat([it["x"].reshape(-1) for it in items]).cpu().pin_memory()
+        ys_n = sum(it["y"].numel() for it in items)
+        ys_host = torch.empty(ys_n, dtype=torch.float16).pin_memory()
+        xs_dev = torch.empty_like(xs_host, device=device)
+        ys_dev = torch.empty(ys_n, dtype=torch.float16, device=device)
+        xo, yo = [], []
+        ox = oy = 0
+        for it in items:
+            xo.append(ox)
+            yo.append(oy)
+            ox += it["x"].numel()
+            oy += it["y"].numel()
+
+        class E2E:
+            def launch(self_, stream_, it):
+                i = it["_i"]
+                arm.launch(stream_, it, xs_dev[xo[i]:].data_ptr(), ys_dev[yo[i]:].data_ptr())
+
+        for i, it in enumerate(items):
+            it["_i"] = i
+
+        def pre():
+            xs_dev.copy_(xs_host, non_blocking=True)
+
+        def post():
+            ys_host.copy_(ys_dev, non_blocking=True)
+
+        ge = capture_step(E2E(), items, stream, allreduce, pre, post)
+        ems, _, _ = time_graph(ge, stream, args.steps, args.warmup, dist_on)
+        e2e = {"value": round(total_bytes / (ems / args.steps / 1e3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(ems / args.steps, 5),
+               "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_n * 2),
+               "path": "af_w8a16_gemv C ABI; pinned-host x -> device, 140 GEMVs, outputs -> pinned host; CUDA graph"}
+    if sampler:
+        sampler.stop()
+
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return 0
+
+    peak, peak_kind = measured_peaks()
+    per_rank_gbs = step_bytes / (ms_step / 1e3) / 1e9
+    out = {
+        "metric": "W8A16 GEMV achieved HBM GB/s (Llama-3.2-3B layer-set stream, M=1)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8e4m3 weights x fp16 act, fp32 accum",
+        "data": "synthetic seeded (W~N(0,0.02) quantised per BASELINE config 0 recipe, x~N(0,1))",
+        "config": config,
+        "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_rank_gbs / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "traffic": traffic_from_profiles(wl, len(items)),
+                     "kernel": "gemv_stream_kernel" if args.impl == "ours" else "w8a16_gemv_kernel (reference)",
+                     "per_launch": f"{step_bytes / len(items) / 1e6:.2f} MB avg algorithmic bytes / launch over "
+                                   f"{ms_step * 1e3 / len(items):.2f} us avg launch (CUDA events over the timed region)"},
+        "gpu_launches": launches if args.impl == "ours" else 0,
+        "clocks": clocks,
+    }
+    if args.impl == "ours":
+        out["e2e"] = e2e
+        if not args.no_cpu_baseline and world == 1 and wl == "layerset":
+            out["cpu_baseline"] = cpu_baseline(items)
+    else:
+        out["impl"] = "reference"
+        out["e2e"] = {"value": out["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        out["cpu_baseline"] = {"value": out["value"], "unit": "GB/s", "cores": None, "kind": "reference",
+                               "sample": "full workload; the reference's path is CUDA (src/kernel/qkv_gemm.cu "
+                                         "w8a16_gemv_kernel, compiled from its sources), run on this GPU"}
+        out["reference_kernel_launches"] = launches
+    print(json.dumps(out))
+    if dist_on:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def traffic_from_profiles(workload, launches_per_step):
+    """DRAM bytes (read + write) per launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload)
+    except Exception:
+        return None
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,102 @@
+/*
+ * atomflow_b200.h -- C ABI of the B200 (sm_100a) W8A16 decode hot path.
+ *
+ * Plain pointers and sizes only.  Every device pointer is owned by the caller;
+ * no entry point allocates device memory.  Every entry point is asynchronous
+ * on `stream` (a cudaStream_t passed as void*, NULL = legacy default stream)
+ * and safe to record under CUDA stream capture once the library has run one
+ * eager call on the device (the first call sets per-kernel attributes).
+ *
+ * Reference interfaces replaced (paths relative to the AtomFlow source tree):
+ *   af_w8a16_gemv    <- launch_w8a16_gemv   include/ops/kernel.h:138-145,
+ *                       src/kernel/qkv_gemm.cu:129-150 (kernel :32-111)
+ *   af_lm_head_gemv  <- the inline cublasGemmEx vocab projection
+ *                       src/core/engine.cu:494-513, fused with the argmax
+ *                       launch at src/core/engine.cu:521
+ *   af_argmax_f32    <- launch_argmax       include/ops/kernel.h:155-159,
+ *                       src/kernel/argmax.cu:92-119
+ * The View-based C++ launchers with the reference's exact signatures are in
+ * atomflow_view_ops.h and forward to these functions.
+ */
+#ifndef ATOMFLOW_B200_H
+#define ATOMFLOW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum af_status {
+    AF_OK = 0,
+    AF_ERR_INVALID = 1,       /* bad shape, dtype, pointer or alignment */
+    AF_ERR_UNSUPPORTED = 2,   /* valid request this build does not implement */
+    AF_ERR_PEER_TIMEOUT = 3,  /* a bounded wait on another rank gave up */
+    AF_ERR_CUDA = 4,          /* a CUDA runtime call failed (see af_last_cuda_error) */
+    AF_ERR_WORKSPACE = 5      /* workspace NULL or smaller than *_workspace_bytes() */
+} af_status;
+
+/* How the FP8 weight rows are scaled. */
+typedef enum af_scale_kind {
+    AF_SCALE_GROUP_F16 = 0,   /* FP16 scales [N, K/group_size], group_size == 128 (reference format) */
+    AF_SCALE_ROW_F32 = 1,     /* FP32 scale per output row [N] */
+    AF_SCALE_NONE = 2         /* no scale (scale 1); `scales` must be NULL */
+} af_scale_kind;
+
+typedef enum af_weight_dtype {
+    AF_W_F16 = 0,             /* FP16 weights (the reference lm_head) */
+    AF_W_FP8_E4M3 = 1         /* FP8-E4M3 weights (OCP E4M3, max 448) */
+} af_weight_dtype;
+
+typedef enum af_argmax_mode {
+    AF_ARGMAX_TRUE = 0,       /* index of the largest logit, ties -> lowest index, NaN ignored */
+    AF_ARGMAX_REF_COMPAT = 1  /* the reference's result: only ids < 65536 are candidates */
+} af_argmax_mode;
+
+const char* af_status_string(af_status s);
+/* Error string of the last CUDA failure seen by this library on this thread. */
+const char* af_last_cuda_error(void);
+int af_version(void);
+
+/* Zero-fills a workspace (required once before its first use; kernels leave it
+ * zeroed again, so a workspace can be reused across calls and graph replays on
+ * one stream).  A workspace must not be shared by calls that may overlap. */
+af_status af_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- GEMV ---
+ * y[m, n] = sum_k dequant(W[n, k]) * x[m, k]   for m < M, n < N
+ *   x : FP16 [M, K] row-major          w : FP8-E4M3 [N, K] row-major
+ *   y : FP16 [M, N] row-major          scales: see af_scale_kind
+ * FP32 accumulation, FP16 round-to-nearest output.  M = 1 is the decode
+ * case of the reference; 1 <= M <= 16 runs in one pass over W, larger M in
+ * ceil(M/16) passes.  Returns AF_ERR_INVALID for group_size != 128 with
+ * AF_SCALE_GROUP_F16, or K % 128 != 0 with group scales (the reference kernel
+ * hard-codes 128-wide groups, qkv_gemm.cu:70). */
+size_t af_w8a16_gemv_workspace_bytes(int M, int N, int K, af_scale_kind kind);
+af_status af_w8a16_gemv(const void* x, const void* w, const void* scales, void* y,
+                        int M, int N, int K, int group_size, af_scale_kind kind,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ lm_head ---
+ * logits[v] = sum_d W[v, d] * x[d]  (FP32 out, one token), optionally
+ * followed by a fused greedy argmax written to *d_argmax (device int).
+ *   w_dtype AF_W_F16      : W FP16 [V, D], row_scale must be NULL
+ *   w_dtype AF_W_FP8_E4M3 : W FP8 [V, D], row_scale FP32 [V]
+ * `logits` may be NULL when only the argmax is wanted; d_argmax may be NULL. */
+size_t af_lm_head_workspace_bytes(int V, int D, af_weight_dtype w_dtype);
+af_status af_lm_head_gemv(const void* x, const void* w, af_weight_dtype w_dtype,
+                          const float* row_scale, float* logits, int V, int D,
+                          int* d_argmax, af_argmax_mode mode,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------- argmax ---
+ * *d_out = argmax(logits[0:V]) (FP32), single launch. */
+size_t af_argmax_workspace_bytes(int V);
+af_status af_argmax_f32(const float* logits, int V, int* d_out, af_argmax_mode mode,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATOMFLOW_B200_H */

@@ -9,30 +9,40 @@
 //
 // Design (one kernel family, three weight formats):
 //   * The weight matrix is cut into 16-row tiles and each tile's K range into
-//     "chunks" (64 FP8 or 32 FP16 positions = 1 KB of one tile).  The grid is
-//     one CTA of 8 warps per SM; the tiles*chunks list is split into equal
-//     contiguous ranges, one per warp, so every warp streams the same number
-//     of bytes whatever N and K are (split-K happens wherever a range boundary
-//     falls inside a tile).
-//   * A lane streams 16 B of two rows per chunk with L1-bypassing 128-bit
-//     loads, four chunks per batch, double-buffered in registers.  The first
-//     batch is issued before griddepcontrol.wait, so with programmatic
-//     dependent launch a GEMV's weight stream starts while the previous kernel
-//     of the stream is still running.
-//   * FP8 bytes become FP16 with the packed cvt (exact), and the dot products
-//     run on the tensor cores as m16n8k16 MMAs with FP32 accumulation: W rows
-//     are the MMA's M, tokens the MMA's N (M = 1 uses column 0; up to 16
-//     tokens share one pass over W).  This leaves ~1 ALU op per weight byte,
-//     far under the issue budget at HBM rate, instead of the reference's
-//     scalar convert-and-FMA chain.
-//   * Group scales are applied to each 64-position partial (one scale group
+//     "chunks" (64 FP8 or 32 FP16 positions = 64 B of each of the 16 rows).
+//     The grid is one CTA per SM; the tiles*chunks list is split into equal
+//     contiguous ranges, one per CTA, so every SM streams the same number of
+//     bytes whatever N and K are.  Split-K happens wherever a range boundary
+//     falls inside a tile.
+//   * Each CTA is one producer warp and eight consumer warps.  The producer
+//     streams "stages" (16 rows x up to 16 chunks = up to 16 KB) into a ring
+//     of shared-memory slots with 1-D bulk copies (cp.async.bulk, one per row)
+//     that complete on per-slot mbarriers.  The producer never reads anything
+//     a previous kernel writes, so it runs ahead of griddepcontrol.wait: with
+//     programmatic dependent launch a GEMV fills its ring (~100 KB per SM, a
+//     whole 3072x3072 GEMV) while the previous kernel of the stream drains.
+//     Two CTAs fit per SM (<= 113 KB shared memory each), one from each of two
+//     consecutive kernels.
+//   * Consumers wait for griddepcontrol.wait, stage x in shared memory, then
+//     take two chunks of every stage each.  FP8 bytes become FP16 with the
+//     packed cvt (exact) and the dot products run on the tensor cores as
+//     m16n8k16 MMAs: W rows are the MMA's M, tokens its N (M = 1 uses one
+//     column; up to 16 tokens share one pass over W).  Every MMA starts from a
+//     zero accumulator and its result is added in FP32 registers, which keeps
+//     cancellation error at the level of an FFMA chain.
+//   * Group scales are applied to each 64-position chunk sum (a scale group
 //     never straddles a chunk); row scales after the reduction.
-//   * Range boundaries inside a tile leave FP32 partials in a workspace;
-//     the last warp to finish a tile (per-tile arrival counter) sums them in
-//     slot order, so the result is deterministic, converts and stores, and
-//     resets the counter for the next call / graph replay.
+//   * At the end of a tile segment the eight warps' partials are summed in
+//     shared memory in warp order.  Segments of a tile split across CTAs leave
+//     FP32 partials in a workspace; the last CTA to finish the tile
+//     (per-tile arrival counter) sums them in slot order -- so results are
+//     deterministic -- stores the output and resets the counter for the next
+//     call / graph replay.
 //   * The lm_head variant writes FP32 logits and folds the greedy argmax into
-//     the epilogue (per-warp candidates, last warp reduces).
+//     the epilogue (per-CTA candidates, the last CTA reduces).
+//   * Every mbarrier wait is bounded (globaltimer); a wait that gives up sets a
+//     sticky error word in the workspace and the kernel unwinds without
+//     breaking its barrier protocol.
 
 #include <cuda_fp8.h>
 #include <cstdio>
@@ -47,11 +57,13 @@ namespace af {
 
 enum WKind { W_FP8_GROUP = 0, W_FP8_ROW = 1, W_F16 = 2 };
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kNB = 4;                 // chunks per register batch
-constexpr int kXsPad = 32;             // halves of padding per staged x row (bank spread)
-constexpr size_t kXsMaxBytes = 100 * 1024;
+constexpr int kCW = 8;                       // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;     // + one producer warp
+constexpr int kStageChunks = 16;             // chunks per stage
+constexpr int kRowPitch = kStageChunks * 64 + 64;   // staged row pitch: == 64 (mod 128) -> conflict-free LDS.128
+constexpr int kSlotBytes = 16 * kRowPitch;   // one stage: 16 rows
+constexpr int kXsPad = 32;                   // halves of padding per staged x row (bank spread)
+constexpr int kMaxStages = 8;
 
 struct GemvParams {
     const uint8_t* w;
@@ -62,82 +74,162 @@ struct GemvParams {
     int tiles, cpt;       // 16-row tiles, chunks per tile
     long long C;          // tiles * cpt
     int ms;               // partial slots per tile
-    int xs_stride;        // staged x row stride (halves)
+    int ns;               // ring stages
+    int xs_stride;        // staged x row stride in halves (0: read x from global)
+    int xs_bytes;         // shared bytes reserved for x
     int y_f32;
     int* cnt;             // [tiles] arrival counters (zero between calls)
     float* part;          // [tiles][ms][32 lanes][4*NT]
     int* arg_out;         // fused argmax result (null: off)
-    float* arg_val;       // [total warps]
-    int* arg_idx;         // [total warps]
+    float* arg_val;       // [CTAs]
+    int* arg_idx;         // [CTAs]
     int* arg_done;        // [1]
     int arg_limit;        // rows >= arg_limit are not argmax candidates
+    int* status;          // sticky error word (bit 0: a bounded wait gave up)
+    unsigned long long wait_ns;
 };
 
 __device__ __forceinline__ uint32_t u4w(const uint4& v, int t) {
     return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
 }
 
-template <int WK, int NT, bool XS>
+struct Stage {
+    long long cur;   // first chunk (global index)
+    int tile, kc0, n;
+};
+
+__device__ __forceinline__ Stage stage_at(long long cur, long long c1, int cpt) {
+    Stage st;
+    st.cur = cur;
+    st.tile = (int)(cur / cpt);
+    st.kc0 = (int)(cur - (long long)st.tile * cpt);
+    int n = kStageChunks;
+    if (cpt - st.kc0 < n) n = cpt - st.kc0;
+    if (c1 - cur < n) n = (int)(c1 - cur);
+    st.n = n;
+    return st;
+}
+
+template <int WK, int NT>
 __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvParams p) {
     constexpr int POS = (WK == W_F16) ? 32 : 64;   // positions per chunk
     constexpr int LPOS = POS / 4;                  // positions per lane per row
-    constexpr int ESZ = (WK == W_F16) ? 2 : 1;     // weight bytes per element
     constexpr int XU4 = LPOS / 8;                  // uint4 of x per lane per chunk
+    constexpr int MT = 8 * NT;                     // token columns
 
     pdl_launch_dependents();
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    __half* xs = reinterpret_cast<__half*>(smem_raw);
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* ring = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + (size_t)p.ns * kSlotBytes);
+    float* red = reinterpret_cast<float*>(smem + (size_t)p.ns * kSlotBytes + p.xs_bytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(red) +
+                                                 (size_t)kCW * 16 * MT * sizeof(float));
+    volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * p.ns);
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + p.ns);
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int g = lane >> 2;
     const int c = lane & 3;
-    const long long GW = (long long)gridDim.x * kWarps;
-    const long long gw = (long long)blockIdx.x * kWarps + warp;
-    // Partition over GWe = min(warps, chunks) warps so that every warp that owns
-    // part of a tile owns at least one chunk of it (the per-tile arrival count
-    // below relies on this); warps beyond GWe stream nothing.
-    const long long GWe = GW < p.C ? GW : p.C;
-    const long long c0 = gw < GWe ? gw * p.C / GWe : p.C;
-    const long long c1 = gw < GWe ? (gw + 1) * p.C / GWe : p.C;
-    const size_t row_bytes = (size_t)p.K * ESZ;
-    const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
+    const long long G = gridDim.x;
+    const long long Ge = G < p.C ? G : p.C;   // CTAs that own chunks (each owns >= 1)
+    const long long cta = blockIdx.x;
+    const long long c0 = cta < Ge ? cta * p.C / Ge : p.C;
+    const long long c1 = cta < Ge ? (cta + 1) * p.C / Ge : p.C;
+    const size_t row_bytes = (size_t)p.K * ((WK == W_F16) ? 2 : 1);
 
-    uint4 wa[kNB][2], wb[kNB][2];
-    uint32_t sa[kNB], sb[kNB];   // FP16 scales of rows g (low) and g+8 (high)
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.ns; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kCW);
+        }
+        *s_abort = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
 
-    auto issue = [&](uint4 (&wbuf)[kNB][2], uint32_t (&sbuf)[kNB], long long cur, int& n,
-                     int& tile, int& kc0) {
-        tile = (int)(cur / p.cpt);
-        kc0 = (int)(cur - (long long)tile * p.cpt);
-        long long left = c1 - cur;
-        n = kNB;
-        if (p.cpt - kc0 < n) n = p.cpt - kc0;
-        if (left < n) n = (int)left;
-        const int r0 = min(tile * 16 + g, p.N - 1);
-        const int r1 = min(tile * 16 + g + 8, p.N - 1);
-        const uint8_t* p0 = p.w + (size_t)r0 * row_bytes + (size_t)(kc0 * POS + c * LPOS) * ESZ;
-        const uint8_t* p1 = p.w + (size_t)r1 * row_bytes + (size_t)(kc0 * POS + c * LPOS) * ESZ;
-#pragma unroll
-        for (int i = 0; i < kNB; ++i) {
-            if (i < n) {
-                wbuf[i][0] = ldg_stream(p0 + (size_t)i * POS * ESZ);
-                wbuf[i][1] = ldg_stream(p1 + (size_t)i * POS * ESZ);
-                if (WK == W_FP8_GROUP) {
-                    const int grp = (kc0 + i) >> 1;   // 64-position chunk -> 128-wide group
-                    sbuf[i] = (uint32_t)__ldg(s16 + (size_t)r0 * p.G + grp) |
-                              ((uint32_t)__ldg(s16 + (size_t)r1 * p.G + grp) << 16);
-                }
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+        const uint64_t lim = *s_abort ? 0ull : p.wait_ns;
+        if (!mbar_wait_bounded(bar, parity, lim)) {
+            if (!*s_abort) {
+                *s_abort = 1;
+                atomicOr(p.status, 1);
             }
         }
     };
 
-    auto load_x = [&](int tok, int pos, uint32_t (&xf)[2 * LPOS / 4]) {
-        // 2*LPOS/4 = LPOS/2 half2 registers = positions [pos, pos + LPOS)
+    if (warp == kCW) {
+        // ------------------------------------------------------ producer ---
+        long long cur = c0;
+        int j = 0;
+        while (cur < c1) {
+            const Stage st = stage_at(cur, c1, p.cpt);
+            const int s = j % p.ns;
+            const int round = j / p.ns;
+            if (round > 0) wait(empty0 + 8 * s, (round - 1) & 1);
+            if (*s_abort) break;
+            const uint32_t bytes = (uint32_t)st.n * 64u;
+            if (lane == 0) mbar_arrive_expect_tx(full0 + 8 * s, 16u * bytes);
+            __syncwarp();
+            if (lane < 16) {
+                const int row = min(st.tile * 16 + lane, p.N - 1);
+                const uint8_t* src = p.w + (size_t)row * row_bytes + (size_t)st.kc0 * 64;
+                bulk_g2s(smem_u32(ring + (size_t)s * kSlotBytes + lane * kRowPitch), src, bytes, full0 + 8 * s);
+            }
+            cur += st.n;
+            ++j;
+        }
+        // Do not leave while copies into this CTA's shared memory may still land.
+        for (int k = (j > p.ns ? j - p.ns : 0); k < j; ++k) wait(full0 + 8 * (k % p.ns), (k / p.ns) & 1);
+        return;
+    }
+
+    // -------------------------------------------------------- consumers ---
+    const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
+
+    auto load_scales = [&](const Stage& st, uint32_t (&sc)[2]) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int i = warp + q * kCW;
+            sc[q] = 0;
+            if (WK == W_FP8_GROUP && i < st.n) {
+                const int grp = (st.kc0 + i) >> 1;
+                const int r0 = min(st.tile * 16 + g, p.N - 1);
+                const int r1 = min(st.tile * 16 + g + 8, p.N - 1);
+                sc[q] = (uint32_t)__ldg(s16 + (size_t)r0 * p.G + grp) |
+                        ((uint32_t)__ldg(s16 + (size_t)r1 * p.G + grp) << 16);
+            }
+        }
+    };
+
+    Stage st{};
+    uint32_t sc[2] = {0, 0};
+    if (c0 < c1) {
+        st = stage_at(c0, c1, p.cpt);
+        load_scales(st, sc);
+    }
+
+    // Everything above touched only weights.  From here on we read the
+    // activations and the workspace, which the previous kernel may own.
+    pdl_wait();
+
+    if (p.xs_stride > 0) {
+        const int k8 = p.K >> 3;
+        const int total = p.M * k8;
+        for (int i = threadIdx.x; i < total; i += kCW * 32) {
+            const int tok = i / k8;
+            const int kk = (i - tok * k8) * 8;
+            *reinterpret_cast<uint4*>(xs + (size_t)tok * p.xs_stride + kk) = ldcg_u4(p.x + (size_t)tok * p.K + kk);
+        }
+        named_bar_sync(1, kCW * 32);
+    }
+
+    auto load_x = [&](int tok, int pos, uint32_t (&xf)[LPOS / 2]) {
 #pragma unroll
         for (int u = 0; u < XU4; ++u) {
             uint4 v;
-            if (XS)
+            if (p.xs_stride > 0)
                 v = *reinterpret_cast<const uint4*>(xs + (size_t)tok * p.xs_stride + pos + u * 8);
             else
                 v = ldcg_u4(p.x + (size_t)tok * p.K + pos + u * 8);
@@ -148,62 +240,68 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
         }
     };
 
-    auto compute = [&](const uint4 (&wbuf)[kNB][2], const uint32_t (&sbuf)[kNB], int n, int kc0,
-                       float (&acc)[NT][4]) {
+    float acc[NT][4];
 #pragma unroll
-        for (int i = 0; i < kNB; ++i) {
-            if (i < n) {
-                const int pos = (kc0 + i) * POS + c * LPOS;
-                uint32_t xf[NT][LPOS / 2];
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
-                if (WK == W_F16) {
+        for (int k = 0; k < 4; ++k) acc[nt][k] = 0.f;
+
+    // One chunk of a staged slot: rows g and g+8, 16 bytes each.
+    auto do_chunk = [&](const unsigned char* slot, int i, int kc, uint32_t scp) {
+        const uint4 w0 = *reinterpret_cast<const uint4*>(slot + g * kRowPitch + i * 64 + c * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(slot + (g + 8) * kRowPitch + i * 64 + c * 16);
+        const int pos = kc * POS + c * LPOS;
+        uint32_t xf[NT][LPOS / 2];
 #pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const uint32_t a0 = u4w(wbuf[i][0], 2 * t), a1 = u4w(wbuf[i][1], 2 * t);
-                        const uint32_t a2 = u4w(wbuf[i][0], 2 * t + 1), a3 = u4w(wbuf[i][1], 2 * t + 1);
+        for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
+        float d[NT][4];
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma16816(acc[nt], a0, a1, a2, a3, xf[nt][2 * t], xf[nt][2 * t + 1]);
-                    }
-                } else {
-                    float d[NT][4];
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+            for (int k = 0; k < 4; ++k) d[nt][k] = 0.f;
+        constexpr int KSTEPS = (WK == W_F16) ? 2 : 4;
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) d[nt][j] = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const uint32_t w0 = u4w(wbuf[i][0], t), w1 = u4w(wbuf[i][1], t);
-                        const uint32_t a0 = e4m3x2_lo(w0), a1 = e4m3x2_lo(w1);
-                        const uint32_t a2 = e4m3x2_hi(w0), a3 = e4m3x2_hi(w1);
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-                            mma16816(d[nt], a0, a1, a2, a3, xf[nt][2 * t], xf[nt][2 * t + 1]);
-                    }
-                    if (WK == W_FP8_GROUP) {
-                        const float s0 = half_bits_to_float((uint16_t)(sbuf[i] & 0xffffu));
-                        const float s1 = half_bits_to_float((uint16_t)(sbuf[i] >> 16));
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
-                            acc[nt][0] = fmaf(s0, d[nt][0], acc[nt][0]);
-                            acc[nt][1] = fmaf(s0, d[nt][1], acc[nt][1]);
-                            acc[nt][2] = fmaf(s1, d[nt][2], acc[nt][2]);
-                            acc[nt][3] = fmaf(s1, d[nt][3], acc[nt][3]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) acc[nt][j] += d[nt][j];
-                    }
-                }
+        for (int t = 0; t < KSTEPS; ++t) {
+            uint32_t a0, a1, a2, a3;
+            if (WK == W_F16) {
+                a0 = u4w(w0, 2 * t);
+                a1 = u4w(w1, 2 * t);
+                a2 = u4w(w0, 2 * t + 1);
+                a3 = u4w(w1, 2 * t + 1);
+            } else {
+                const uint32_t b0 = u4w(w0, t), b1 = u4w(w1, t);
+                a0 = e4m3x2_lo(b0);
+                a1 = e4m3x2_lo(b1);
+                a2 = e4m3x2_hi(b0);
+                a3 = e4m3x2_hi(b1);
             }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float e[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(e, a0, a1, a2, a3, xf[nt][2 * t], xf[nt][2 * t + 1]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) d[nt][k] += e[k];
+            }
+        }
+        if (WK == W_FP8_GROUP) {
+            const float s0 = half_bits_to_float((uint16_t)(scp & 0xffffu));
+            const float s1 = half_bits_to_float((uint16_t)(scp >> 16));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] = fmaf(s0, d[nt][0], acc[nt][0]);
+                acc[nt][1] = fmaf(s0, d[nt][1], acc[nt][1]);
+                acc[nt][2] = fmaf(s1, d[nt][2], acc[nt][2]);
+                acc[nt][3] = fmaf(s1, d[nt][3], acc[nt][3]);
+            }
+        } else {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[nt][k] += d[nt][k];
         }
     };
 
-    // Fused-argmax running best of this lane.
-    float best_v = 0.f;
+    float best_v = 0.f;   // fused argmax: running best of this lane (warp 0)
     int best_i = -1;
 
     auto emit = [&](int tile, float (&v)[NT][4]) {
@@ -225,17 +323,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int tok = nt * 8 + 2 * c + j;
+                for (int jj = 0; jj < 2; ++jj) {
+                    const int tok = nt * 8 + 2 * c + jj;
                     if (tok < p.M) {
                         if (p.y_f32) {
                             float* y = static_cast<float*>(p.y) + (size_t)tok * p.N;
-                            if (r0 < p.N) y[r0] = v[nt][j];
-                            if (r1 < p.N) y[r1] = v[nt][2 + j];
+                            if (r0 < p.N) y[r0] = v[nt][jj];
+                            if (r1 < p.N) y[r1] = v[nt][2 + jj];
                         } else {
                             __half* y = static_cast<__half*>(p.y) + (size_t)tok * p.N;
-                            if (r0 < p.N) y[r0] = __float2half_rn(v[nt][j]);
-                            if (r1 < p.N) y[r1] = __float2half_rn(v[nt][2 + j]);
+                            if (r0 < p.N) y[r0] = __float2half_rn(v[nt][jj]);
+                            if (r1 < p.N) y[r1] = __float2half_rn(v[nt][2 + jj]);
                         }
                     }
                 }
@@ -248,22 +346,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
         }
     };
 
-    auto finish_tile = [&](int tile, float (&acc)[NT][4]) {
+    // Warp 0 only: combine this CTA's sum for `tile` with other CTAs' segments.
+    auto finish_tile = [&](int tile, float (&v)[NT][4]) {
         const long long start = (long long)tile * p.cpt;
         const long long end = start + p.cpt;
-        const long long own_a = ((start + 1) * GWe - 1) / p.C;   // warp owning chunk `start`
-        const long long own_b = (end * GWe - 1) / p.C;           // warp owning chunk `end - 1`
+        const long long own_a = ((start + 1) * Ge - 1) / p.C;   // CTA owning chunk `start`
+        const long long own_b = (end * Ge - 1) / p.C;           // CTA owning chunk `end - 1`
         const int count = (int)(own_b - own_a + 1);
         if (count == 1) {
-            emit(tile, acc);
+            emit(tile, v);
             return;
         }
-        const int slot = (int)(gw - own_a);
+        const int slot = (int)(cta - own_a);
         float* dst = p.part + (((size_t)tile * p.ms + slot) * 32 + lane) * 4 * NT;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-            __stcg(reinterpret_cast<float4*>(dst + 4 * nt),
-                   make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+            __stcg(reinterpret_cast<float4*>(dst + 4 * nt), make_float4(v[nt][0], v[nt][1], v[nt][2], v[nt][3]));
         __threadfence();
         __syncwarp();
         int last = 0;
@@ -271,80 +369,90 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) return;
         __threadfence();
-        float v[NT][4];
+        float r[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) v[nt][j] = 0.f;
-        for (int s = 0; s < count; ++s) {
-            const float* src = p.part + (((size_t)tile * p.ms + s) * 32 + lane) * 4 * NT;
+            for (int k = 0; k < 4; ++k) r[nt][k] = 0.f;
+        for (int sl = 0; sl < count; ++sl) {
+            const float* src = p.part + (((size_t)tile * p.ms + sl) * 32 + lane) * 4 * NT;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float4 f = ldcg_f4(src + 4 * nt);
-                v[nt][0] += f.x;
-                v[nt][1] += f.y;
-                v[nt][2] += f.z;
-                v[nt][3] += f.w;
+                r[nt][0] += f.x;
+                r[nt][1] += f.y;
+                r[nt][2] += f.z;
+                r[nt][3] += f.w;
             }
         }
         if (lane == 0) p.cnt[tile] = 0;
-        emit(tile, v);
+        emit(tile, r);
     };
 
-    long long cur = c0;
-    int nA = 0, tA = 0, kA = 0, nB = 0, tB = 0, kB = 0;
-    if (cur < c1) issue(wa, sa, cur, nA, tA, kA);
-
-    // Everything above touched only weights and scales.  From here on we read
-    // the activations and the workspace, which the previous kernel may own.
-    pdl_wait();
-
-    if (XS) {
-        const int k8 = p.K >> 3;
-        const int total = p.M * k8;
-        for (int i = threadIdx.x; i < total; i += kThreads) {
-            const int tok = i / k8;
-            const int kk = (i - tok * k8) * 8;
-            *reinterpret_cast<uint4*>(xs + (size_t)tok * p.xs_stride + kk) =
-                ldcg_u4(p.x + (size_t)tok * p.K + kk);
-        }
-        __syncthreads();
-    }
-
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
-
-    auto reset_acc = [&]() {
+    // All consumer warps: sum the eight warps' partials of `tile` in warp order.
+    auto tile_end = [&](int tile) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[nt][j] = 0.f;
+            for (int jj = 0; jj < 2; ++jj) {
+                const int tok = nt * 8 + 2 * c + jj;
+                red[(warp * 16 + g) * MT + tok] = acc[nt][jj];
+                red[(warp * 16 + g + 8) * MT + tok] = acc[nt][2 + jj];
+            }
+        named_bar_sync(1, kCW * 32);
+        float v[NT][4];
+        if (warp == 0) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    const int tok = nt * 8 + 2 * c + jj;
+                    float a = 0.f, b = 0.f;
+                    for (int w = 0; w < kCW; ++w) {
+                        a += red[(w * 16 + g) * MT + tok];
+                        b += red[(w * 16 + g + 8) * MT + tok];
+                    }
+                    v[nt][jj] = a;
+                    v[nt][2 + jj] = b;
+                }
+        }
+        named_bar_sync(1, kCW * 32);
+        if (warp == 0) finish_tile(tile, v);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[nt][k] = 0.f;
     };
 
+    long long cur = c0;
+    int j = 0;
     while (cur < c1) {
-        long long nxt = cur + nA;
-        if (nxt < c1) issue(wb, sb, nxt, nB, tB, kB);
-        compute(wa, sa, nA, kA, acc);
-        if (nxt == c1 || kA + nA == p.cpt) {
-            finish_tile(tA, acc);
-            reset_acc();
+        Stage nx{};
+        uint32_t scn[2] = {0, 0};
+        const bool has_next = cur + st.n < c1;
+        if (has_next) {
+            nx = stage_at(cur + st.n, c1, p.cpt);
+            load_scales(nx, scn);   // one stage ahead: hides the scale loads' latency
         }
-        cur = nxt;
-        if (cur >= c1) break;
-        nxt = cur + nB;
-        if (nxt < c1) issue(wa, sa, nxt, nA, tA, kA);
-        compute(wb, sb, nB, kB, acc);
-        if (nxt == c1 || kB + nB == p.cpt) {
-            finish_tile(tB, acc);
-            reset_acc();
+        const int s = j % p.ns;
+        wait(full0 + 8 * s, (j / p.ns) & 1);
+        const unsigned char* slot = ring + (size_t)s * kSlotBytes;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int i = warp + q * kCW;
+            if (i < st.n) do_chunk(slot, i, st.kc0 + i, sc[q]);
         }
-        cur = nxt;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        if (st.kc0 + st.n == p.cpt || cur + st.n == c1) tile_end(st.tile);
+        cur += st.n;
+        ++j;
+        st = nx;
+        sc[0] = scn[0];
+        sc[1] = scn[1];
     }
 
-    if (p.arg_out != nullptr) {
+    if (p.arg_out != nullptr && warp == 0) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
@@ -353,17 +461,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
         }
         int last = 0;
         if (lane == 0) {
-            __stcg(p.arg_val + gw, best_v);
-            __stcg(p.arg_idx + gw, best_i);
+            __stcg(p.arg_val + cta, best_v);
+            __stcg(p.arg_idx + cta, best_i);
             __threadfence();
-            last = (atomicAdd(p.arg_done, 1) == (int)GW - 1);
+            last = (atomicAdd(p.arg_done, 1) == (int)G - 1);
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
             __threadfence();
             float bv = 0.f;
             int bi = -1;
-            for (long long i = lane; i < GW; i += 32) {
+            for (long long i = lane; i < G; i += 32) {
                 const float v = ldcg_f32(p.arg_val + i);
                 const int ix = ldcg_s32(p.arg_idx + i);
                 if (argmax_better(v, ix, bv, bi)) { bv = v; bi = ix; }
@@ -384,6 +492,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
 
 // Any alignment, any K: one warp per (row, token), scalar decode.  Used when a
 // pointer or K does not meet the streaming kernel's 16-byte layout rules.
+__device__ __forceinline__ uint16_t ld_u16_bytes(const void* base, size_t byte_off) {
+    const uint8_t* b = static_cast<const uint8_t*>(base) + byte_off;
+    return (uint16_t)(b[0] | (b[1] << 8));
+}
+
 __global__ void gemv_simple_kernel(const uint8_t* w, int w_f16, const void* s, int skind, int G,
                                    const __half* x, void* y, int y_f32, int M, int N, int K) {
     pdl_wait();
@@ -396,37 +509,35 @@ __global__ void gemv_simple_kernel(const uint8_t* w, int w_f16, const void* s, i
     for (int k = lane; k < K; k += 32) {
         float wv;
         if (w_f16) {
-            __half h;
-            memcpy(&h, w + ((size_t)n * K + k) * 2, 2);
-            wv = __half2float(h);
+            wv = half_bits_to_float(ld_u16_bytes(w, ((size_t)n * K + k) * 2));
         } else {
             const __half_raw hr = __nv_cvt_fp8_to_halfraw(w[(size_t)n * K + k], __NV_E4M3);
             wv = __half2float(__half(hr));
         }
-        if (skind == AF_SCALE_GROUP_F16) {
-            uint16_t sb;
-            memcpy(&sb, static_cast<const uint8_t*>(s) + ((size_t)n * G + k / 128) * 2, 2);
-            wv *= half_bits_to_float(sb);
-        }
-        __half xh;
-        memcpy(&xh, reinterpret_cast<const uint8_t*>(x) + ((size_t)m * K + k) * 2, 2);
-        acc = fmaf(wv, __half2float(xh), acc);
+        if (skind == AF_SCALE_GROUP_F16) wv *= half_bits_to_float(ld_u16_bytes(s, ((size_t)n * G + k / 128) * 2));
+        acc = fmaf(wv, half_bits_to_float(ld_u16_bytes(x, ((size_t)m * K + k) * 2)), acc);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) {
         if (skind == AF_SCALE_ROW_F32 && s != nullptr) {
-            float sv;
-            memcpy(&sv, static_cast<const uint8_t*>(s) + (size_t)n * 4, 4);
-            acc *= sv;
+            const uint8_t* sb = static_cast<const uint8_t*>(s) + (size_t)n * 4;
+            acc *= __uint_as_float((uint32_t)sb[0] | ((uint32_t)sb[1] << 8) | ((uint32_t)sb[2] << 16) |
+                                   ((uint32_t)sb[3] << 24));
         }
+        uint8_t* yb = static_cast<uint8_t*>(y);
         if (y_f32) {
-            uint8_t* dst = static_cast<uint8_t*>(y) + ((size_t)m * N + n) * 4;
-            memcpy(dst, &acc, 4);
+            const uint32_t b = __float_as_uint(acc);
+            uint8_t* dst = yb + ((size_t)m * N + n) * 4;
+            dst[0] = b & 0xff;
+            dst[1] = (b >> 8) & 0xff;
+            dst[2] = (b >> 16) & 0xff;
+            dst[3] = b >> 24;
         } else {
-            const __half h = __float2half_rn(acc);
-            uint8_t* dst = static_cast<uint8_t*>(y) + ((size_t)m * N + n) * 2;
-            memcpy(dst, &h, 2);
+            const uint16_t b = __half_as_ushort(__float2half_rn(acc));
+            uint8_t* dst = yb + ((size_t)m * N + n) * 2;
+            dst[0] = b & 0xff;
+            dst[1] = b >> 8;
         }
     }
 }
@@ -441,77 +552,95 @@ struct Plan {
     int tiles, cpt;
     long long C;
     int ms;
-    size_t off_cnt, off_done, off_argv, off_argi, off_part, total;
+    size_t off_status, off_cnt, off_done, off_argv, off_argi, off_part, total;
 };
 
 Plan make_plan(int nt, int N, int K, int wk, int sms) {
     Plan pl{};
     pl.nt = nt;
     pl.grid = sms * ctas_per_sm();
-    const long long GW = (long long)pl.grid * kWarps;
+    const long long G = pl.grid;
     const int pos = (wk == W_F16) ? 32 : 64;
     pl.tiles = (N + 15) / 16;
     pl.cpt = K / pos;
     pl.C = (long long)pl.tiles * pl.cpt;
-    // Every active warp owns q or q+1 chunks (q >= 1), so a tile of cpt chunks
-    // is split among at most 1 + ceil((cpt - 1) / q) warps.
-    const long long GWe = GW < pl.C ? GW : (pl.C > 0 ? pl.C : 1);
-    const long long q = pl.C / GWe;
+    // Every active CTA owns q or q+1 chunks (q >= 1), so a tile of cpt chunks
+    // is split among at most 1 + ceil((cpt - 1) / q) CTAs.
+    const long long Ge = G < pl.C ? G : (pl.C > 0 ? pl.C : 1);
+    const long long q = pl.C / Ge;
     long long ms = q > 0 ? 1 + (pl.cpt - 1 + q - 1) / q : pl.cpt;
     pl.ms = (int)(ms < pl.cpt ? ms : pl.cpt);
     if (pl.ms < 1) pl.ms = 1;
     size_t off = 0;
+    pl.off_status = off;
+    off = round_up(off + 4, 256);
     pl.off_cnt = off;
     off = round_up(off + (size_t)pl.tiles * 4, 256);
     pl.off_done = off;
     off = round_up(off + 4, 256);
     pl.off_argv = off;
-    off = round_up(off + (size_t)GW * 4, 256);
+    off = round_up(off + (size_t)G * 4, 256);
     pl.off_argi = off;
-    off = round_up(off + (size_t)GW * 4, 256);
+    off = round_up(off + (size_t)G * 4, 256);
     pl.off_part = off;
     off = round_up(off + (size_t)pl.tiles * pl.ms * 32 * 4 * nt * sizeof(float), 256);
     pl.total = off;
     return pl;
 }
 
-template <int WK, int NT, bool XS>
+// Shared memory per CTA: two CTAs (of consecutive kernels) must fit on one SM.
+size_t smem_budget() {
+    static size_t v = [] {
+        const char* e = getenv("AF_SMEM_BUDGET_KB");
+        long k = e ? atol(e) : 113;
+        if (k < 40 || k > 226) k = 113;
+        return (size_t)k * 1024;
+    }();
+    return v;
+}
+
+unsigned long long wait_limit_ns() {
+    static unsigned long long v = [] {
+        const char* e = getenv("AF_WAIT_LIMIT_MS");
+        long long ms = e ? atoll(e) : 2000;
+        if (ms < 1) ms = 2000;
+        return (unsigned long long)ms * 1000000ull;
+    }();
+    return v;
+}
+
+template <int WK, int NT>
 cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    auto kern = gemv_stream_kernel<WK, NT, XS>;
+    auto kern = gemv_stream_kernel<WK, NT>;
     static std::once_flag flags[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaError_t attr_err = cudaSuccess;
+    static cudaError_t attr_err[kMaxDevices];
     std::call_once(flags[dev % kMaxDevices], [&] {
-        attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)kXsMaxBytes + 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        attr_err[dev % kMaxDevices] = e;
     });
-    if (attr_err != cudaSuccess) return attr_err;
+    if (attr_err[dev % kMaxDevices] != cudaSuccess) return attr_err[dev % kMaxDevices];
     return launch_pdl(kern, dim3(pl.grid), dim3(kThreads), smem, st, prm);
 }
 
-template <int WK>
-cudaError_t dispatch_stream(const GemvParams& prm, const Plan& pl, bool xs, size_t smem,
-                            cudaStream_t st) {
-    if (pl.nt == 1)
-        return xs ? launch_stream<WK, 1, true>(prm, pl, smem, st)
-                  : launch_stream<WK, 1, false>(prm, pl, 0, st);
-    return xs ? launch_stream<WK, 2, true>(prm, pl, smem, st)
-              : launch_stream<WK, 2, false>(prm, pl, 0, st);
-}
-
-cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, bool xs, size_t smem,
-                     cudaStream_t st) {
+cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
+    const bool two = pl.nt == 2;
     switch (wk) {
-        case W_FP8_GROUP: return dispatch_stream<W_FP8_GROUP>(prm, pl, xs, smem, st);
-        case W_FP8_ROW: return dispatch_stream<W_FP8_ROW>(prm, pl, xs, smem, st);
-        default: return dispatch_stream<W_F16>(prm, pl, xs, smem, st);
+        case W_FP8_GROUP:
+            return two ? launch_stream<W_FP8_GROUP, 2>(prm, pl, smem, st) : launch_stream<W_FP8_GROUP, 1>(prm, pl, smem, st);
+        case W_FP8_ROW:
+            return two ? launch_stream<W_FP8_ROW, 2>(prm, pl, smem, st) : launch_stream<W_FP8_ROW, 1>(prm, pl, smem, st);
+        default:
+            return two ? launch_stream<W_F16, 2>(prm, pl, smem, st) : launch_stream<W_F16, 1>(prm, pl, smem, st);
     }
 }
 
 // Whether the streaming kernel's layout rules hold; otherwise the scalar kernel runs.
-bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* y, int K,
-               int y_f32) {
+bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* y, int K, int y_f32) {
     const int pos = (wk == W_F16) ? 32 : 64;
     if (K <= 0 || K % pos != 0) return false;
     if (!aligned(x, 16) || !aligned(w, 16)) return false;
@@ -522,18 +651,16 @@ bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* 
 }
 
 // Runs one pass of <= 16 tokens.
-af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, void* y, int y_f32,
-                   int M, int N, int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes,
-                   cudaStream_t st) {
+af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, void* y, int y_f32, int M, int N,
+                   int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes, cudaStream_t st) {
     int sms = device_sm_count();
     if (sms <= 0) return AF_ERR_CUDA;
     if (!stream_ok(wk, x, w, s, y, K, y_f32) || (arg_out != nullptr && M != 1)) {
         if (arg_out != nullptr) return AF_ERR_UNSUPPORTED;
-        const int skind = (wk == W_FP8_GROUP) ? AF_SCALE_GROUP_F16
-                          : (wk == W_FP8_ROW) ? AF_SCALE_ROW_F32 : AF_SCALE_NONE;
+        const int skind = (wk == W_FP8_GROUP) ? AF_SCALE_GROUP_F16 : (wk == W_FP8_ROW) ? AF_SCALE_ROW_F32 : AF_SCALE_NONE;
         dim3 grid((N + 7) / 8, M);
-        cudaError_t e = launch_pdl(gemv_simple_kernel, grid, dim3(256), 0, st, w, (int)(wk == W_F16),
-                                   s, skind, K / 128, x, y, y_f32, M, N, K);
+        cudaError_t e = launch_pdl(gemv_simple_kernel, grid, dim3(256), 0, st, w, (int)(wk == W_F16), s, skind,
+                                   K / 128, x, y, y_f32, M, N, K);
         return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_simple_kernel");
     }
     const int nt = (M <= 8) ? 1 : 2;
@@ -554,8 +681,8 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     prm.cpt = pl.cpt;
     prm.C = pl.C;
     prm.ms = pl.ms;
-    prm.xs_stride = K + kXsPad;
     prm.y_f32 = y_f32;
+    prm.status = reinterpret_cast<int*>(wsb + pl.off_status);
     prm.cnt = reinterpret_cast<int*>(wsb + pl.off_cnt);
     prm.part = reinterpret_cast<float*>(wsb + pl.off_part);
     prm.arg_out = arg_out;
@@ -563,9 +690,22 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     prm.arg_idx = reinterpret_cast<int*>(wsb + pl.off_argi);
     prm.arg_done = reinterpret_cast<int*>(wsb + pl.off_done);
     prm.arg_limit = arg_limit;
-    const size_t smem = (size_t)M * (K + kXsPad) * sizeof(__half);
-    const bool xs = smem <= kXsMaxBytes;
-    cudaError_t e = dispatch(wk, prm, pl, xs, xs ? smem : 0, st);
+    prm.wait_ns = wait_limit_ns();
+    // Shared memory: ring stages, staged x (when it leaves room for >= 3 stages),
+    // the cross-warp reduction buffer and the mbarriers.
+    const size_t budget = smem_budget();
+    const size_t red = (size_t)kCW * 16 * (8 * nt) * sizeof(float);
+    const size_t fixed = red + 2 * kMaxStages * 8 + 16;
+    size_t xs = round_up((size_t)M * (K + kXsPad) * sizeof(__half), 128);
+    if (fixed + xs + 3 * (size_t)kSlotBytes > budget) xs = 0;
+    size_t ns = (budget - fixed - xs) / kSlotBytes;
+    if (ns > (size_t)kMaxStages) ns = kMaxStages;
+    if (ns < 2) return AF_ERR_UNSUPPORTED;
+    prm.ns = (int)ns;
+    prm.xs_stride = xs ? K + kXsPad : 0;
+    prm.xs_bytes = (int)xs;
+    const size_t smem = ns * kSlotBytes + xs + red + 2 * ns * 8 + 16;
+    cudaError_t e = dispatch(wk, prm, pl, smem, st);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_stream_kernel");
 }
 

@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(kArgThreads) argmax_kernel(const float* __rest
         const float bv = ldcg_f32(ws.val + b);
         const int bi = ldcg_s32(ws.idx + b);
         if (argmax_better(bv, bi, v, i)) { v = bv; i = bi; }
+        __stcg(ws.val + b, 0.f);   // leave the workspace all-zero: any op may reuse it next
+        __stcg(ws.idx + b, 0);
     }
     block_best(v, i);
     if (threadIdx.x == 0) {

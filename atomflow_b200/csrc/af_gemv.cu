@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
 #pragma unroll
             for (int k = 0; k < 4; ++k) r[nt][k] = 0.f;
         for (int sl = 0; sl < count; ++sl) {
-            const float* src = p.part + (((size_t)tile * p.ms + sl) * 32 + lane) * 4 * NT;
+            float* src = p.part + (((size_t)tile * p.ms + sl) * 32 + lane) * 4 * NT;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float4 f = ldcg_f4(src + 4 * nt);
@@ -383,6 +383,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
                 r[nt][1] += f.y;
                 r[nt][2] += f.z;
                 r[nt][3] += f.w;
+                // leave the workspace all-zero: any op may reuse it next
+                __stcg(reinterpret_cast<float4*>(src + 4 * nt), make_float4(0.f, 0.f, 0.f, 0.f));
             }
         }
         if (lane == 0) p.cnt[tile] = 0;
@@ -475,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream_kernel(const GemvPara
                 const float v = ldcg_f32(p.arg_val + i);
                 const int ix = ldcg_s32(p.arg_idx + i);
                 if (argmax_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+                __stcg(p.arg_val + i, 0.f);
+                __stcg(p.arg_idx + i, 0);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {

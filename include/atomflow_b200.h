@@ -59,9 +59,11 @@ const char* af_status_string(af_status s);
 const char* af_last_cuda_error(void);
 int af_version(void);
 
-/* Zero-fills a workspace (required once before its first use; kernels leave it
- * zeroed again, so a workspace can be reused across calls and graph replays on
- * one stream).  A workspace must not be shared by calls that may overlap. */
+/* Zero-fills a workspace.  Required once before its first use: every kernel
+ * returns all the workspace bytes it touched to zero before it exits (unless a
+ * bounded wait gave up -- then word 0 holds a non-zero error code), so one
+ * workspace serves any sequence of calls, ops and shapes, graph replays
+ * included, provided the calls cannot overlap on the GPU (same stream). */
 af_status af_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- GEMV ---

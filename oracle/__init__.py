@@ -49,6 +49,7 @@ def cpu():
         L.af_oracle_quantize_gs128.argtypes = [vp, i, i, vp, vp]
         L.af_oracle_quantize_row.argtypes = [vp, i, i, vp, vp]
         L.af_oracle_gemv_f64.argtypes = [vp, vp, vp, i, i, i, i, vp]
+        L.af_oracle_gemv_f64_l2.argtypes = [vp, vp, vp, i, i, i, i, vp, vp]
         L.af_oracle_gemv_refmath.argtypes = [vp, vp, vp, i, i, vp, i]
         L.af_oracle_argmax.restype = i
         L.af_oracle_argmax.argtypes = [vp, i, i]
@@ -99,17 +100,20 @@ def quantize_row(w):
 KIND = {"group": 0, "row": 1, "none": 2, "f16": 3}
 
 
-def gemv_f64(x, w, s, kind):
-    """x fp16-bits uint16 [M, K]; w uint8 [N, K] (or uint16 fp16 bits for kind 'f16')."""
+def gemv_f64(x, w, s, kind, with_l2=False):
+    """x fp16-bits uint16 [M, K]; w uint8 [N, K] (or uint16 fp16 bits for kind 'f16').
+    Returns y [M, N] in FP64 (and, with_l2, the l2 norm of each output's terms)."""
     x = np.ascontiguousarray(x, dtype=np.uint16)
     x = x.reshape(-1, x.shape[-1])
     w = np.ascontiguousarray(w)
     M, K = x.shape
     N = w.shape[0]
     y = np.empty((M, N), np.float64)
-    sp = _p(np.ascontiguousarray(s)) if s is not None else None
-    cpu().af_oracle_gemv_f64(_p(x), _p(w), sp, KIND[kind], M, N, K, _p(y))
-    return y
+    l2 = np.empty((M, N), np.float64) if with_l2 else None
+    s = np.ascontiguousarray(s) if s is not None else None
+    cpu().af_oracle_gemv_f64_l2(_p(x), _p(w), _p(s) if s is not None else None, KIND[kind], M, N, K,
+                                _p(y), _p(l2) if with_l2 else None)
+    return (y, l2) if with_l2 else y
 
 
 def gemv_refmath(x, w, s, nthreads=1):

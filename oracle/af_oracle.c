@@ -135,6 +135,11 @@ void af_oracle_quantize_row(const float* w, int N, int K, uint8_t* q, float* s) 
 
 void af_oracle_gemv_f64(const uint16_t* x, const void* w, const void* s, int kind, int M, int N,
                         int K, double* y) {
+    af_oracle_gemv_f64_l2(x, w, s, kind, M, N, K, y, NULL);
+}
+
+void af_oracle_gemv_f64_l2(const uint16_t* x, const void* w, const void* s, int kind, int M, int N,
+                           int K, double* y, double* l2) {
     const uint8_t* w8 = (const uint8_t*)w;
     const uint16_t* w16 = (const uint16_t*)w;
     const uint16_t* sg = (const uint16_t*)s;
@@ -143,7 +148,7 @@ void af_oracle_gemv_f64(const uint16_t* x, const void* w, const void* s, int kin
 #pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
         for (int m = 0; m < M; ++m) {
-            double acc = 0.0;
+            double acc = 0.0, sq = 0.0;
             for (int k = 0; k < K; ++k) {
                 double wv;
                 if (kind == 3)
@@ -151,10 +156,16 @@ void af_oracle_gemv_f64(const uint16_t* x, const void* w, const void* s, int kin
                 else
                     wv = af_oracle_e4m3_to_float(w8[(size_t)n * K + k]);
                 if (kind == 0) wv *= af_oracle_half_to_float(sg[(size_t)n * G + k / 128]);
-                acc += wv * (double)af_oracle_half_to_float(x[(size_t)m * K + k]);
+                const double t = wv * (double)af_oracle_half_to_float(x[(size_t)m * K + k]);
+                acc += t;
+                sq += t * t;
             }
-            if (kind == 1) acc *= (double)sr[n];
+            if (kind == 1) {
+                acc *= (double)sr[n];
+                sq *= (double)sr[n] * (double)sr[n];
+            }
             y[(size_t)m * N + n] = acc;
+            if (l2) l2[(size_t)m * N + n] = sqrt(sq);
         }
     }
 }

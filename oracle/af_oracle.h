@@ -39,6 +39,10 @@ void af_oracle_quantize_row(const float* w, int N, int K, uint8_t* q, float* s);
  * kind 2: FP8 W, no scale; 3: FP16 W (bits), no scale. */
 void af_oracle_gemv_f64(const uint16_t* x, const void* w, const void* s, int kind, int M, int N,
                         int K, double* y);
+/* As af_oracle_gemv_f64, also returning l2[m,n] = sqrt(sum_k (W[n,k]*scale*x[m,k])^2),
+ * the natural scale of the FP32 rounding noise of any FP32-accumulated result. */
+void af_oracle_gemv_f64_l2(const uint16_t* x, const void* w, const void* s, int kind, int M, int N,
+                           int K, double* y, double* l2);
 
 /* Bit-exact restatement of src/kernel/qkv_gemm.cu:32-111 (w8a16_gemv_kernel<256>)
  * for one token: FP32 fused multiply-add per element in the kernel's thread /

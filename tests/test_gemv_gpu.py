@@ -68,14 +68,14 @@ SHAPES = [(3072, 3072), (5120, 3072), (8192, 3072), (3072, 8192),
 def test_gemv_m1_group_full_shapes(N, K):
     x, q, s = make_gemv_case(100 + N % 97 + K % 89, 1, N, K)
     y = gemv_np(x, q, s)
-    assert_fp16_parity(y, oracle.gemv_f64(x, q, s, "group"), f"{N}x{K}", oracle.gemv_refmath(x, q, s, 8))
+    assert_fp16_parity(y, oracle.gemv_f64(x, q, s, "group", with_l2=True), f"{N}x{K}", oracle.gemv_refmath(x, q, s, 8))
 
 
 @pytest.mark.parametrize("N,K", [(1, 128), (3, 128), (17, 256), (31, 384), (1000, 640),
                                  (129, 1152), (4099, 512), (2, 8192), (300, 14336)])
 def test_gemv_ragged_shapes(N, K):
     x, q, s = make_gemv_case(7 + N + K, 1, N, K)
-    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group"), f"{N}x{K}",
+    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group", with_l2=True), f"{N}x{K}",
                        oracle.gemv_refmath(x, q, s, 8))
 
 
@@ -85,7 +85,7 @@ def test_gemv_batched_tokens(M, N, K):
     x, q, s = make_gemv_case(900 + M, M, N, K)
     # the reference kernel is M = 1 only: each token row through its restatement
     rk = np.stack([oracle.gemv_refmath(x[m], q, s, 8) for m in range(M)])
-    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group"), f"M={M} {N}x{K}", rk)
+    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group", with_l2=True), f"M={M} {N}x{K}", rk)
 
 
 @pytest.mark.parametrize("kind", ["row", "none"])
@@ -93,7 +93,7 @@ def test_gemv_batched_tokens(M, N, K):
 def test_gemv_row_scale_and_unscaled(kind, M, N, K):
     x, q, s = make_gemv_case(31 + M + N, M, N, K, kind=kind)
     y = gemv_np(x, q, s, kind)
-    assert_fp16_parity(y, oracle.gemv_f64(x, q, s, kind), f"{kind} M={M} {N}x{K}")
+    assert_fp16_parity(y, oracle.gemv_f64(x, q, s, kind, with_l2=True), f"{kind} M={M} {N}x{K}")
 
 
 @pytest.mark.parametrize("x_std", [1e-3, 40.0, 250.0])
@@ -102,7 +102,7 @@ def test_gemv_heavy_tailed_and_small_activations(x_std):
     x = x.copy()
     x[0, ::97] = fp16_bits(np.float32(287.8))      # outliers like gt_layer27_mlp_out
     x[0, 5::211] = 0
-    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group"), f"x_std={x_std}",
+    assert_fp16_parity(gemv_np(x, q, s), oracle.gemv_f64(x, q, s, "group", with_l2=True), f"x_std={x_std}",
                        oracle.gemv_refmath(x, q, s, 8))
 
 
@@ -122,7 +122,7 @@ def test_gemv_matches_reference_kernel_and_pins_refmath():
         np.testing.assert_array_equal(oracle.gemv_refmath(x, q, s), yref)
         # and ours is within 2 FP16 ulp of the reference kernel's output as well as of FP64
         y = gemv_np(x, q, s)
-        ref64 = oracle.gemv_f64(x, q, s, "group")[0]
+        ref64 = oracle.gemv_f64(x, q, s, "group", with_l2=True)
         assert_fp16_parity(y, ref64, "vs reference kernel / f64", yref)
         yv = y.view(np.float16).astype(np.float64)
         rv = yref.view(np.float16).astype(np.float64)
@@ -157,11 +157,11 @@ def test_gemv_linearity_full_size():
     x3 = fp16_bits(x.view(np.float16).astype(np.float32).sum(0, keepdims=True))
     xa = np.concatenate([x, x3])
     y = gemv_np(xa, q, s).view(np.float16).astype(np.float64)
-    ref = oracle.gemv_f64(xa, q, s, "group")
+    ref = oracle.gemv_f64(xa, q, s, "group", with_l2=True)
     rk = np.stack([oracle.gemv_refmath(xa[m], q, s, 8) for m in range(3)])
     assert_fp16_parity(y.astype(np.float16).view(np.uint16), ref, "linearity", rk)
     lhs, rhs = y[2], y[0] + y[1]
-    scale = np.sqrt(np.mean(ref[2] ** 2))
+    scale = np.sqrt(np.mean(ref[0][2] ** 2))
     assert np.abs(lhs - rhs).max() <= 0.01 * scale
 
 
@@ -176,7 +176,7 @@ def test_gemv_fallback_paths_unaligned():
     rc, y = run_gemv(x, q, s, xd=xbuf[1:], qd=qbuf[3:])
     torch.cuda.synchronize()
     assert rc == 0
-    assert_fp16_parity(y.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, s, "group"), "unaligned",
+    assert_fp16_parity(y.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, s, "group", with_l2=True), "unaligned",
                        oracle.gemv_refmath(x, q, s))
 
 
@@ -222,4 +222,5 @@ def test_gemv_graph_replay_and_pdl_chain():
     for i, o in enumerate(outs):
         np.testing.assert_array_equal(o.cpu().numpy(), eager[i])
     y0 = eager[0].view(np.uint16)
-    assert_fp16_parity(y0, oracle.gemv_f64(cases[0][0], cases[0][1], cases[0][2], "group"), "graph")
+    assert_fp16_parity(y0, oracle.gemv_f64(cases[0][0], cases[0][1], cases[0][2], "group", with_l2=True), "graph",
+                       oracle.gemv_refmath(cases[0][0], cases[0][1], cases[0][2]))

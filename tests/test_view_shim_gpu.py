@@ -29,7 +29,7 @@ def test_launch_w8a16_gemv_view():
     L.launch_w8a16_gemv(ctypes.byref(vx), ctypes.byref(vw), ctypes.byref(vs), ctypes.byref(vy), 128, st)
     torch.cuda.synchronize()
     assert L.af_view_last_status() == 0
-    assert_fp16_parity(yd.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, s, "group"), "view")
+    assert_fp16_parity(yd.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, s, "group", with_l2=True), "view")
     # a wrong dtype is rejected, recorded, and launches nothing
     vbad = make_view(qd.data_ptr(), DataType.FP16, [N, K])
     L.launch_w8a16_gemv(ctypes.byref(vx), ctypes.byref(vbad), ctypes.byref(vs), ctypes.byref(vy), 128, st)
@@ -60,4 +60,4 @@ def test_launch_argmax_and_linear_gemm_view():
     L.launch_linear_gemm(ctypes.byref(vi), ctypes.byref(vw), ctypes.byref(vo), None, st)
     torch.cuda.synchronize()
     assert L.af_view_last_status() == 0
-    assert_fp16_parity(yd.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, None, "none"), "linear")
+    assert_fp16_parity(yd.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, None, "none", with_l2=True), "linear")

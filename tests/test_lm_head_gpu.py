@@ -116,3 +116,17 @@ def test_argmax_standalone(V):
                                    torch.cuda.current_stream().cuda_stream) == 0
             torch.cuda.synchronize()
             assert int(out.item()) == oracle.argmax(v, mode)
+
+
+def test_lm_head_needs_its_argmax_workspace():
+    L = lib()
+    V, D = 4096, 3072
+    x, w = f16_case(3, V, D)
+    xd, wd = dev(x), dev(w)
+    logits = torch.zeros(V, dtype=torch.float32, device="cuda")
+    idx = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.af_lm_head_workspace_bytes(V, D, 0) > 0
+    rc = L.af_lm_head_gemv(xd.data_ptr(), wd.data_ptr(), 0, None, logits.data_ptr(), V, D, idx.data_ptr(), 0,
+                           None, 0, st)
+    assert rc == 5   # AF_ERR_WORKSPACE

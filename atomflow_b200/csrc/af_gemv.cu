@@ -15,13 +15,16 @@
 //     rows past the share are neither loaded nor stored), and each tile's K
 //     range is cut into "chunks" of 64 FP8 / 32 FP16 positions (64 B per row).
 //   * The CTA's tiles x chunks list is split into equal contiguous ranges, one
-//     per warp.  A warp streams its range with L1-bypassing 128-bit loads: a
-//     lane loads 16 B of each of two rows (g, g+8) per chunk together with the
-//     chunk's two group scales, two chunks per batch, double-buffered in
-//     registers.  The first batch is issued before griddepcontrol.wait, so with
-//     programmatic dependent launch the weight stream starts while the
-//     previous kernel of the stream drains; for <= 8 tokens a CTA is capped at
-//     64 registers per thread so that a CTA of the next GEMV fits beside it.
+//     per warp.  A lane streams exactly the bytes it consumes -- 16 B of each
+//     of two rows (g, g+8) per chunk -- with 16-byte asynchronous copies
+//     (cp.async, L2 only) into its own places of a 10-chunk shared-memory ring
+//     (160 KB per SM in flight), one commit group per chunk; the CTA's group
+//     scales are staged the same way.  No lane reads another lane's bytes, so
+//     the ring needs no barriers.  The ring is filled before
+//     griddepcontrol.wait: with programmatic dependent launch a config-sized
+//     GEMV's whole weight share is requested while the previous kernel of the
+//     stream drains, and the stream costs one DRAM round trip, not one per
+//     batch.
 //   * FP8 bytes become FP16 with the packed cvt (exact) and the dot products
 //     run on the tensor cores as m16n8k16 MMAs: W rows are the MMA's M, tokens
 //     its N (M = 1 uses one column; up to 16 tokens share one pass over W).
@@ -62,6 +65,7 @@ struct GemvParams {
     int cpt;              // chunks per 16-row tile
     int xs_stride;        // staged x row stride in halves (0: read x from global)
     int xs_bytes;         // shared bytes reserved for x
+    int sc_bytes;         // shared bytes reserved for staged group scales (0: read from L2)
     int y_f32;
     int* arg_out;         // fused argmax result (null: off)
     float* arg_val;       // [CTAs]
@@ -89,8 +93,8 @@ __device__ __forceinline__ long long owner_of(long long c, long long n, long lon
     return ((c + 1) * parts - 1) / n;
 }
 
-template <int WK, int NT, int kWarps, int kNB, int kMinCtas>
-__global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(const GemvParams p) {
+template <int WK, int NT, int kWarps, int kS>
+__global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int POS = (WK == W_F16) ? 32 : 64;   // positions per chunk
     constexpr int LPOS = POS / 4;                  // positions per lane per row
@@ -106,8 +110,11 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
     TRACE(0);
     pdl_launch_dependents();
     extern __shared__ __align__(128) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
-    float* wslots = reinterpret_cast<float*>(smem + p.xs_bytes);   // [kWarps][2][32][PF]
+    // [ring: kWarps x kS chunk slots of 1 KB][x: xs_bytes][scales: sc_bytes][warp partials]
+    unsigned char* ring = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + (size_t)kWarps * kS * 1024);
+    unsigned char* scs = smem + (size_t)kWarps * kS * 1024 + p.xs_bytes;
+    float* wslots = reinterpret_cast<float*>(scs + p.sc_bytes);   // [kWarps][2][32][PF]
     __shared__ float s_best_v[kWarps];
     __shared__ int s_best_i[kWarps];
 
@@ -129,38 +136,51 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
     const size_t row_bytes = (size_t)p.K * ESZ;
     const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
 
-    uint4 wa[kNB][2], wb[kNB][2];
-    uint32_t sa[kNB], sb[kNB];   // FP16 scales of rows g (low) and g+8 (high)
+    // The CTA's group scales are one contiguous block of the [N, G] array:
+    // stage it (16-byte pieces covering it) when the caller's layout allows.
+    const size_t sc_lo = p.sc_bytes ? ((size_t)row0 * p.G * 2) & ~(size_t)15 : 0;
+    if (WK == W_FP8_GROUP && p.sc_bytes) {
+        const size_t sc_hi = ((size_t)row1 * p.G * 2 + 15) & ~(size_t)15;
+        const unsigned char* sb = static_cast<const unsigned char*>(p.s);
+        for (size_t o = sc_lo + (size_t)threadIdx.x * 16; o < sc_hi; o += (size_t)kThreads * 16)
+            cp_async16(smem_u32(scs + (o - sc_lo)), sb + o);
+    }
+    cp_async_commit();
 
-    // Rows past row1 are not loaded (zeros): only real rows are streamed.
-    auto issue = [&](uint4 (&wbuf)[kNB][2], uint32_t (&sbuf)[kNB], int cur, int& n, int& tile, int& kc0) {
-        tile = cur / p.cpt;
-        kc0 = cur - tile * p.cpt;
-        n = kNB;
-        if (p.cpt - kc0 < n) n = p.cpt - kc0;
-        if (wc1 - cur < n) n = wc1 - cur;
-        const int r0 = row0 + tile * 16 + g;
-        const int r1 = r0 + 8;
-        const bool v0 = r0 < row1, v1 = r1 < row1;
-        const uint8_t* p0 = p.w + (size_t)(v0 ? r0 : row0) * row_bytes + (size_t)(kc0 * POS + c * LPOS) * ESZ;
-        const uint8_t* p1 = p.w + (size_t)(v1 ? r1 : row0) * row_bytes + (size_t)(kc0 * POS + c * LPOS) * ESZ;
-#pragma unroll
-        for (int i = 0; i < kNB; ++i) {
-            if (i < n) {
-                wbuf[i][0] = v0 ? ldg_stream(p0 + (size_t)i * POS * ESZ) : make_uint4(0, 0, 0, 0);
-                wbuf[i][1] = v1 ? ldg_stream(p1 + (size_t)i * POS * ESZ) : make_uint4(0, 0, 0, 0);
-                if (WK == W_FP8_GROUP) {
-                    const int grp = (kc0 + i) >> 1;   // 64-position chunk -> 128-wide group
-                    sbuf[i] = (v0 ? (uint32_t)__ldg(s16 + (size_t)r0 * p.G + grp) : 0u) |
-                              ((v1 ? (uint32_t)__ldg(s16 + (size_t)r1 * p.G + grp) : 0u) << 16);
-                }
+    // Each lane streams exactly the bytes it consumes: per chunk 16 B of row g
+    // and 16 B of row g+8 into its own places of a kS-slot ring, one commit
+    // group per chunk.  Rows past row1 are not loaded.
+    unsigned char* my_ring = ring + (size_t)warp * kS * 1024;
+    // Issue cursor: next chunk to request (tile, chunk-in-tile, ring slot),
+    // advanced incrementally -- no divisions in the stream loop.
+    int i_left = wc1 - wc0;
+    int i_tile = wc0 / p.cpt, i_kc = wc0 - (wc0 / p.cpt) * p.cpt, i_slot = 0;
+    const uint8_t* i_p0 = nullptr;
+    const uint8_t* i_p1 = nullptr;
+    auto i_rows = [&]() {   // per-tile row pointers (null: row past row1)
+        const int r0 = row0 + i_tile * 16 + g;
+        i_p0 = r0 < row1 ? p.w + (size_t)r0 * row_bytes + (size_t)c * LPOS * ESZ : nullptr;
+        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * row_bytes + (size_t)c * LPOS * ESZ : nullptr;
+    };
+    i_rows();
+    auto issue = [&]() {
+        if (i_left > 0) {
+            unsigned char* slot = my_ring + (size_t)i_slot * 1024;
+            const size_t off = (size_t)i_kc * POS * ESZ;
+            if (i_p0) cp_async16(smem_u32(slot + lane * 16), i_p0 + off);
+            if (i_p1) cp_async16(smem_u32(slot + 512 + lane * 16), i_p1 + off);
+            --i_left;
+            if (++i_slot == kS) i_slot = 0;
+            if (++i_kc == p.cpt) {
+                i_kc = 0;
+                ++i_tile;
+                i_rows();
             }
         }
+        cp_async_commit();   // empty groups past the end keep the count uniform
     };
-
-    int cur = wc0;
-    int nA = 0, tA = 0, kA = 0, nB = 0, tB = 0, kB = 0;
-    if (cur < wc1) issue(wa, sa, cur, nA, tA, kA);
+#pragma unroll 1
+    for (int q = 0; q < kS; ++q) issue();
 
     // Everything above touched only weights.  From here on we read the
     // activations and write outputs, which the previous kernel may own.
@@ -176,6 +196,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
             *reinterpret_cast<uint4*>(xs + (size_t)tok * p.xs_stride + kk) = ldcg_u4(p.x + (size_t)tok * p.K + kk);
         }
     }
+    cp_async_wait<kS>();   // the scale group (the oldest) has landed
     __syncthreads();
     TRACE(2);
 
@@ -200,60 +221,78 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
 #pragma unroll
         for (int k = 0; k < 4; ++k) acc[nt][k] = 0.f;
 
-    auto compute = [&](const uint4 (&wbuf)[kNB][2], const uint32_t (&sbuf)[kNB], int n, int kc0) {
+    auto scale_pair = [&](int r0, int r1, int grp) -> uint32_t {
+        uint32_t lo = 0, hi = 0;
+        if (p.sc_bytes) {
+            if (r0 < row1) lo = *reinterpret_cast<const uint16_t*>(scs + ((size_t)r0 * p.G + grp) * 2 - sc_lo);
+            if (r1 < row1) hi = *reinterpret_cast<const uint16_t*>(scs + ((size_t)r1 * p.G + grp) * 2 - sc_lo);
+        } else {
+            if (r0 < row1) lo = __ldg(s16 + (size_t)r0 * p.G + grp);
+            if (r1 < row1) hi = __ldg(s16 + (size_t)r1 * p.G + grp);
+        }
+        return lo | (hi << 16);
+    };
+
+    // Chunk at (tile, kc, slot): its data landed (wait_group); compute, then
+    // refill the slot with the chunk kS further on.
+    auto compute = [&](int tile, int kc, int slot_i) {
+        const int r0 = row0 + tile * 16 + g;
+        const int r1 = r0 + 8;
+        const unsigned char* slot = my_ring + (size_t)slot_i * 1024;
+        cp_async_wait<kS - 1>();
+        const uint4 w0 = r0 < row1 ? *reinterpret_cast<const uint4*>(slot + lane * 16) : make_uint4(0, 0, 0, 0);
+        const uint4 w1 = r1 < row1 ? *reinterpret_cast<const uint4*>(slot + 512 + lane * 16) : make_uint4(0, 0, 0, 0);
+        const uint32_t scp = (WK == W_FP8_GROUP) ? scale_pair(r0, r1, kc >> 1) : 0u;
+        const int pos = kc * POS + c * LPOS;
+        uint32_t xf[NT][LPOS / 2];
 #pragma unroll
-        for (int i = 0; i < kNB; ++i) {
-            if (i < n) {
-                const int pos = (kc0 + i) * POS + c * LPOS;
-                uint32_t xf[NT][LPOS / 2];
+        for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
+        float d[NT][4];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
-                float d[NT][4];
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+            for (int k = 0; k < 4; ++k) d[nt][k] = 0.f;
+        constexpr int KSTEPS = (WK == W_F16) ? 2 : 4;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) d[nt][k] = 0.f;
-                constexpr int KSTEPS = (WK == W_F16) ? 2 : 4;
-#pragma unroll
-                for (int t = 0; t < KSTEPS; ++t) {
-                    uint32_t a0, a1, a2, a3;
-                    if (WK == W_F16) {
-                        a0 = u4w(wbuf[i][0], 2 * t);
-                        a1 = u4w(wbuf[i][1], 2 * t);
-                        a2 = u4w(wbuf[i][0], 2 * t + 1);
-                        a3 = u4w(wbuf[i][1], 2 * t + 1);
-                    } else {
-                        const uint32_t b0 = u4w(wbuf[i][0], t), b1 = u4w(wbuf[i][1], t);
-                        a0 = e4m3x2_lo(b0);
-                        a1 = e4m3x2_lo(b1);
-                        a2 = e4m3x2_hi(b0);
-                        a3 = e4m3x2_hi(b1);
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        float e[4] = {0.f, 0.f, 0.f, 0.f};
-                        mma16816(e, a0, a1, a2, a3, xf[nt][2 * t], xf[nt][2 * t + 1]);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) d[nt][k] += e[k];
-                    }
-                }
-                if (WK == W_FP8_GROUP) {
-                    const float s0 = half_bits_to_float((uint16_t)(sbuf[i] & 0xffffu));
-                    const float s1 = half_bits_to_float((uint16_t)(sbuf[i] >> 16));
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        acc[nt][0] = fmaf(s0, d[nt][0], acc[nt][0]);
-                        acc[nt][1] = fmaf(s0, d[nt][1], acc[nt][1]);
-                        acc[nt][2] = fmaf(s1, d[nt][2], acc[nt][2]);
-                        acc[nt][3] = fmaf(s1, d[nt][3], acc[nt][3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) acc[nt][k] += d[nt][k];
-                }
+        for (int t = 0; t < KSTEPS; ++t) {
+            uint32_t a0, a1, a2, a3;
+            if (WK == W_F16) {
+                a0 = u4w(w0, 2 * t);
+                a1 = u4w(w1, 2 * t);
+                a2 = u4w(w0, 2 * t + 1);
+                a3 = u4w(w1, 2 * t + 1);
+            } else {
+                const uint32_t b0 = u4w(w0, t), b1 = u4w(w1, t);
+                a0 = e4m3x2_lo(b0);
+                a1 = e4m3x2_lo(b1);
+                a2 = e4m3x2_hi(b0);
+                a3 = e4m3x2_hi(b1);
             }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float e[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(e, a0, a1, a2, a3, xf[nt][2 * t], xf[nt][2 * t + 1]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) d[nt][k] += e[k];
+            }
+        }
+        // the slot's bytes are in registers and used: refill it
+        issue();
+        if (WK == W_FP8_GROUP) {
+            const float s0 = half_bits_to_float((uint16_t)(scp & 0xffffu));
+            const float s1 = half_bits_to_float((uint16_t)(scp >> 16));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                acc[nt][0] = fmaf(s0, d[nt][0], acc[nt][0]);
+                acc[nt][1] = fmaf(s0, d[nt][1], acc[nt][1]);
+                acc[nt][2] = fmaf(s1, d[nt][2], acc[nt][2]);
+                acc[nt][3] = fmaf(s1, d[nt][3], acc[nt][3]);
+            }
+        } else {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[nt][k] += d[nt][k];
         }
     };
 
@@ -305,6 +344,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
     // A warp's range has at most two partial tile segments: its first (slot 0)
     // and its last (slot 1); a range inside one tile uses slot 0.
     const int first_tile = wc0 < wc1 ? wc0 / p.cpt : -1;
+
     auto segment_end = [&](int tile, int seg_lo, int seg_hi) {
         if (seg_lo == tile * p.cpt && seg_hi == (tile + 1) * p.cpt) {
             emit(tile, acc);   // the whole tile lies in this warp's range
@@ -320,26 +360,24 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_stream_kernel(cons
             for (int k = 0; k < 4; ++k) acc[nt][k] = 0.f;
     };
 
-    int seg_lo = cur;
-    while (cur < wc1) {
-        int nxt = cur + nA;
-        if (nxt < wc1) issue(wb, sb, nxt, nB, tB, kB);
-        compute(wa, sa, nA, kA);
-        if (nxt == wc1 || kA + nA == p.cpt) {
-            segment_end(tA, seg_lo, nxt);
-            seg_lo = nxt;
+    int seg_lo = wc0;
+    int c_tile = wc0 < wc1 ? wc0 / p.cpt : 0;
+    int c_kc = wc0 - c_tile * p.cpt, c_slot = 0;
+#pragma unroll 2
+    for (int j = wc0; j < wc1; ++j) {
+        compute(c_tile, c_kc, c_slot);
+        if (++c_slot == kS) c_slot = 0;
+        const bool tile_done = ++c_kc == p.cpt;
+        if (j + 1 == wc1 || tile_done) {
+            segment_end(c_tile, seg_lo, j + 1);
+            seg_lo = j + 1;
         }
-        cur = nxt;
-        if (cur >= wc1) break;
-        nxt = cur + nB;
-        if (nxt < wc1) issue(wa, sa, nxt, nA, tA, kA);
-        compute(wb, sb, nB, kB);
-        if (nxt == wc1 || kB + nB == p.cpt) {
-            segment_end(tB, seg_lo, nxt);
-            seg_lo = nxt;
+        if (tile_done) {
+            c_kc = 0;
+            ++c_tile;
         }
-        cur = nxt;
     }
+    cp_async_wait<0>();
     TRACE(3);
     __syncthreads();
     TRACE(4);
@@ -503,20 +541,12 @@ Plan make_plan(int nt, int N, int K, int wk, int sms, bool argmax) {
     return pl;
 }
 
-// Kernel shape: AF_GEMV_VARIANT=0..3 selects one for tuning experiments.
-int gemv_variant() {
-    static int v = [] {
-        const char* e = getenv("AF_GEMV_VARIANT");
-        int k = e ? atoi(e) : 0;
-        return (k >= 0 && k <= 3) ? k : 0;
-    }();
-    return v;
-}
-int variant_warps(int v) { return v == 1 ? 32 : 16; }
+constexpr int kWarpsPerCta = 16;
+constexpr int kRingSlots = 10;   // chunk slots per warp (1 KB each)
 
-template <int WK, int NT, int WPB, int NB, int MINC>
-cudaError_t launch_stream_v(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    auto kern = gemv_stream_kernel<WK, NT, WPB, NB, MINC>;
+template <int WK, int NT>
+cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
+    auto kern = gemv_stream_kernel<WK, NT, kWarpsPerCta, kRingSlots>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -529,20 +559,7 @@ cudaError_t launch_stream_v(const GemvParams& prm, const Plan& pl, size_t smem, 
         attr_err[dev % kMaxDevices] = e;
     });
     if (attr_err[dev % kMaxDevices] != cudaSuccess) return attr_err[dev % kMaxDevices];
-    return launch_pdl(kern, dim3(pl.grid), dim3(WPB * 32), smem, st, prm);
-}
-
-// Variant 0 (default): 16 warps, 2-chunk batches; for <= 8 tokens capped at
-// 64 registers so that a CTA of the next kernel fits beside it on the SM.
-// 1: 32 warps; 2: 16 warps with 4-chunk batches; 3: variant 0 without the cap.
-template <int WK, int NT>
-cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    switch (gemv_variant()) {
-        case 1: return launch_stream_v<WK, NT, 32, 2, 1>(prm, pl, smem, st);
-        case 2: return launch_stream_v<WK, NT, 16, 4, 1>(prm, pl, smem, st);
-        case 3: return launch_stream_v<WK, NT, 16, 2, 1>(prm, pl, smem, st);
-        default: return launch_stream_v<WK, NT, 16, 2, NT == 1 ? 2 : 1>(prm, pl, smem, st);
-    }
+    return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
 cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
@@ -606,15 +623,22 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         prm.arg_done = reinterpret_cast<int*>(wsb + pl.off_done);
     }
     prm.arg_limit = arg_limit;
-    // Shared memory: staged x (when it fits) and the per-warp partial slots.
-    const size_t slots = (size_t)variant_warps(gemv_variant()) * 2 * 32 * 4 * nt * sizeof(float);
+    // Shared memory: the ring, staged x and scales (when they fit), warp partials.
+    const size_t ring = (size_t)kWarpsPerCta * kRingSlots * 1024;
+    const size_t slots = (size_t)kWarpsPerCta * 2 * 32 * 4 * nt * sizeof(float);
+    const size_t budget = kSmemMax - 1024;   // static shared and alignment
+    size_t sc = 0;
+    if (wk == W_FP8_GROUP && aligned(s, 16) && ((size_t)N * (K / 128) * 2) % 16 == 0) {
+        const size_t rows = (size_t)(N + pl.grid - 1) / pl.grid;
+        sc = round_up(rows * (K / 128) * 2 + 32, 128);
+        if (ring + slots + sc > budget || sc > 32 * 1024) sc = 0;
+    }
     size_t xs = round_up((size_t)M * (K + kXsPad) * sizeof(__half), 128);
-    // Keep two CTAs per SM possible: x staging only while the total stays
-    // under ~96 KB, else the activations are read from L2.
-    if (xs + slots > 96 * 1024) xs = 0;
+    if (ring + slots + sc + xs > budget) xs = 0;
     prm.xs_stride = xs ? K + kXsPad : 0;
     prm.xs_bytes = (int)xs;
-    cudaError_t e = dispatch(wk, prm, pl, xs + slots, st);
+    prm.sc_bytes = (int)sc;
+    cudaError_t e = dispatch(wk, prm, pl, ring + xs + sc + slots, st);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_stream_kernel");
 }
 
@@ -626,8 +650,7 @@ int wkind_of(af_scale_kind kind) { return kind == AF_SCALE_GROUP_F16 ? W_FP8_GRO
 using namespace af;
 
 extern "C" size_t af_w8a16_gemv_workspace_bytes(int M, int N, int K, af_scale_kind kind) {
-    // The GEMV needs no device scratch; the size stays part of the ABI so a
-    // future kernel can ask for some without a signature change.
+    // The GEMV needs no device scratch; the size query stays part of the ABI.
     (void)M, (void)N, (void)K, (void)kind;
     return 0;
 }

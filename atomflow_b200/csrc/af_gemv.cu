@@ -93,7 +93,7 @@ __device__ __forceinline__ long long owner_of(long long c, long long n, long lon
     return ((c + 1) * parts - 1) / n;
 }
 
-template <int WK, int NT, int kWarps, int kS>
+template <int WK, int NT, int kWarps, int kS, bool SX>
 __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int POS = (WK == W_F16) ? 32 : 64;   // positions per chunk
@@ -187,7 +187,57 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     pdl_wait();
     TRACE(1);
 
-    if (p.xs_stride > 0) {
+    // SX (one token, FP8 weights): x is re-expressed as four E5M2 pieces in a
+    // common power-of-two scale, x * 2^xe = p0 + p1 + p2 + p3 -- exact for
+    // every FP16 value down to 2^-16 of the largest |x| (4 x 3 significant bits
+    // cover FP16's 11) -- so the FP8 weights feed the tensor cores directly
+    // (e4m3 x e5m2 MMA, FP32 accumulate) with no per-weight conversion.  Piece
+    // q of x lives in row q of xs (stride xs_stride bytes).
+    __shared__ int s_xe;
+    unsigned char* xp = reinterpret_cast<unsigned char*>(xs);
+    if (SX) {
+        float m = 0.f;
+        for (int k = threadIdx.x * 8; k < p.K; k += kThreads * 8) {
+            const uint4 v = ldcg_u4(p.x + k);
+            const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float2 f = __half22float2(h[u]);
+                m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_best_v[warp] = m;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float mm = 0.f;
+            for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, s_best_v[w]);
+            int e = 0;
+            if (mm > 0.f) frexpf(mm, &e);   // mm < 2^e
+            s_xe = 15 - e;                   // max |x| * 2^xe < 2^15 <= E5M2 max
+        }
+        __syncthreads();
+        const int xe = s_xe;
+        for (int k = threadIdx.x * 8; k < p.K; k += kThreads * 8) {
+            const uint4 v = ldcg_u4(p.x + k);
+            const __half* h = reinterpret_cast<const __half*>(&v);
+            uint32_t pk[4][2] = {};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                float r = ldexpf(__half2float(h[u]), xe);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E5M2);
+                    r -= __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E5M2)));
+                    pk[q][u >> 2] |= (uint32_t)b << (8 * (u & 3));
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint2*>(xp + (size_t)q * p.xs_stride + k) = make_uint2(pk[q][0], pk[q][1]);
+        }
+    } else if (p.xs_stride > 0) {
         const int k8 = p.K >> 3;
         const int total = p.M * k8;
         for (int i = threadIdx.x; i < total; i += kThreads) {
@@ -244,15 +294,30 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
         const uint4 w1 = r1 < row1 ? *reinterpret_cast<const uint4*>(slot + 512 + lane * 16) : make_uint4(0, 0, 0, 0);
         const uint32_t scp = (WK == W_FP8_GROUP) ? scale_pair(r0, r1, kc >> 1) : 0u;
         const int pos = kc * POS + c * LPOS;
-        uint32_t xf[NT][LPOS / 2];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
         float d[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int k = 0; k < 4; ++k) d[nt][k] = 0.f;
-        constexpr int KSTEPS = (WK == W_F16) ? 2 : 4;
+        if (SX) {
+            // lane (g, c) supplies MMA column g = x piece g (columns 4..7 are zero)
+            const uint4 xb = g < 4 ? *reinterpret_cast<const uint4*>(xp + (size_t)g * p.xs_stride + pos)
+                                   : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                float e[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16832_e4m3_e5m2(e, u4w(w0, 2 * t), u4w(w1, 2 * t), u4w(w0, 2 * t + 1), u4w(w1, 2 * t + 1),
+                                   u4w(xb, 2 * t), u4w(xb, 2 * t + 1));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) d[0][k] += e[k];
+            }
+        }
+        uint32_t xf[NT][LPOS / 2];
+        if (!SX) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
+        }
+        constexpr int KSTEPS = SX ? 0 : (WK == W_F16) ? 2 : 4;
 #pragma unroll
         for (int t = 0; t < KSTEPS; ++t) {
             uint32_t a0, a1, a2, a3;
@@ -302,6 +367,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     auto emit = [&](int tile, float (&v)[NT][4]) {
         const int r0 = row0 + tile * 16 + g;
         const int r1 = r0 + 8;
+        if (SX) {
+            // columns 0..3 hold the four pieces' sums: lanes c = 0 and 1 each
+            // own two; the total lands in lane c = 0 (token 0), unscaled by 2^-xe
+            float a = v[0][0] + v[0][1], b = v[0][2] + v[0][3];
+            a += __shfl_down_sync(0xffffffffu, a, 1);
+            b += __shfl_down_sync(0xffffffffu, b, 1);
+            const int xe = s_xe;
+            v[0][0] = ldexpf(a, -xe);
+            v[0][2] = ldexpf(b, -xe);
+            v[0][1] = v[0][3] = 0.f;
+        }
         if (WK == W_FP8_ROW && p.s != nullptr) {
             const float* s32 = static_cast<const float*>(p.s);
             const float s0 = r0 < row1 ? __ldg(s32 + r0) : 0.f;
@@ -465,6 +541,305 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     }
 }
 
+// ---------------------------------------------------------------------------
+// One token, FP8 weights, K % 128 == 0: the decode case of the reference
+// (every launch_w8a16_gemv of engine.cu, and an FP8 lm_head).  Same row split
+// and warp ranges as gemv_stream_kernel, tuned for a chain of dependent GEMVs:
+//   * a chunk is a whole 128-wide scale group (a lane streams 32 B of rows g
+//     and g+8), all per-tile addressing is hoisted out of the chunk loop;
+//   * 8 warps and <= 113 KB of shared memory per CTA, so that the CTA of the
+//     NEXT GEMV of the stream sits on the same SM and fills its own ring
+//     (cp.async, before its griddepcontrol.wait) while this one computes --
+//     the SM's memory pipe never idles between kernels;
+//   * x arrives by one bulk copy on the TMA engine straight into shared memory,
+//     so it does not queue behind the co-resident CTA's weight requests.
+template <bool GROUP, int kWarps, int kS>
+__global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvParams p) {
+    constexpr int kThreads = kWarps * 32;
+    constexpr int kSlot = 2048;
+#ifdef AF_EXP_TRACE
+    __shared__ unsigned s_tl;
+    if (threadIdx.x == 0) s_tl = atomicAdd(&g_trace_launch, 1) / gridDim.x;
+    __syncthreads();
+#endif
+    TRACE(0);
+    pdl_launch_dependents();
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char* ring = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + (size_t)kWarps * kS * kSlot);   // x: K halves
+    unsigned char* scs = reinterpret_cast<unsigned char*>(xs) + p.xs_bytes;       // staged scales
+    float* wslots = reinterpret_cast<float*>(scs + p.sc_bytes);                  // [kWarps][2][32][4]
+    __shared__ __align__(8) uint64_t s_xbar;
+    __shared__ float s_red[kWarps];
+    __shared__ int s_redi[kWarps];
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int row0 = (int)((long long)cta * p.N / G);
+    const int row1 = (int)((long long)(cta + 1) * p.N / G);
+    const int cpt = p.K >> 7;                     // chunks (scale groups) per row
+    const int T = (row1 - row0 + 15) >> 4;
+    const int L = T * cpt;
+    const int We = L < kWarps ? L : kWarps;
+    const int wc0 = warp < We ? (int)((long long)warp * L / We) : L;
+    const int wc1 = warp < We ? (int)((long long)(warp + 1) * L / We) : L;
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&s_xbar), 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    // staged scales: bytes [sc_lo, ...) of the [N, G] FP16 array
+    const size_t sc_lo = p.sc_bytes ? ((size_t)row0 * cpt * 2) & ~(size_t)15 : 0;
+    if (GROUP && p.sc_bytes) {
+        const size_t sc_hi = ((size_t)row1 * cpt * 2 + 15) & ~(size_t)15;
+        const unsigned char* sb = static_cast<const unsigned char*>(p.s);
+        for (size_t o = sc_lo + (size_t)threadIdx.x * 16; o < sc_hi; o += (size_t)kThreads * 16)
+            cp_async16(smem_u32(scs + (o - sc_lo)), sb + o);
+    }
+    cp_async_commit();
+
+    // ---- issue cursor (weights only: runs before griddepcontrol.wait) ----
+    // Slot layout: [row g bytes 0-15 | row g 16-31 | row g+8 0-15 | row g+8 16-31],
+    // 512 B each, lane-major: conflict-free 128-bit shared loads.
+    const uint32_t my_ring = smem_u32(ring + (size_t)warp * kS * kSlot) + lane * 16;
+    int i_left = wc1 - wc0;
+    int i_tile = wc0 / (cpt > 0 ? cpt : 1);
+    int i_kc = wc0 - i_tile * cpt, i_slot = 0;
+    const uint8_t* i_p0 = nullptr;
+    const uint8_t* i_p1 = nullptr;
+    auto i_rows = [&]() {
+        const int r0 = row0 + i_tile * 16 + g;
+        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K + c * 32 : nullptr;
+        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K + c * 32 : nullptr;
+    };
+    i_rows();
+    auto issue = [&]() {
+        if (i_left > 0) {
+            const uint32_t d = my_ring + i_slot * kSlot;
+            const int off = i_kc << 7;
+            if (i_p0) {
+                cp_async16(d, i_p0 + off);
+                cp_async16(d + 512, i_p0 + off + 16);
+            }
+            if (i_p1) {
+                cp_async16(d + 1024, i_p1 + off);
+                cp_async16(d + 1536, i_p1 + off + 16);
+            }
+            --i_left;
+            if (++i_slot == kS) i_slot = 0;
+            if (++i_kc == cpt) {
+                i_kc = 0;
+                ++i_tile;
+                i_rows();
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll 1
+    for (int q = 0; q < kS; ++q) issue();
+
+    pdl_wait();
+    TRACE(1);
+    // x by one bulk copy on the TMA engine (see above)
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.K * 2u);
+        bulk_g2s(smem_u32(xs), p.x, (uint32_t)p.K * 2u, smem_u32(&s_xbar));
+    }
+    cp_async_wait<kS>();   // the scale group (the oldest) has landed
+    __syncthreads();       // everyone's staged scales are visible
+    mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
+    TRACE(2);
+
+    // ---- compute cursor ----
+    const unsigned char* my_ring_p = ring + (size_t)warp * kS * kSlot + lane * 16;
+    const __half* my_x = xs + c * 32;
+    const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
+    const float* rs = static_cast<const float*>(p.s);
+    int c_tile = wc0 / (cpt > 0 ? cpt : 1);
+    int c_kc = wc0 - c_tile * cpt, c_slot = 0;
+    bool v0 = false, v1 = false;
+    const uint16_t* sp0 = nullptr;   // scales of rows g, g+8 (shared or global)
+    const uint16_t* sp1 = nullptr;
+    auto c_rows = [&]() {
+        const int r0 = row0 + c_tile * 16 + g;
+        v0 = r0 < row1;
+        v1 = r0 + 8 < row1;
+        if (GROUP) {
+            const int a0 = v0 ? r0 : row0, a1 = v1 ? r0 + 8 : row0;
+            if (p.sc_bytes) {
+                sp0 = reinterpret_cast<const uint16_t*>(scs + (size_t)a0 * cpt * 2 - sc_lo);
+                sp1 = reinterpret_cast<const uint16_t*>(scs + (size_t)a1 * cpt * 2 - sc_lo);
+            } else {
+                sp0 = s16 + (size_t)a0 * cpt;
+                sp1 = s16 + (size_t)a1 * cpt;
+            }
+        }
+    };
+    c_rows();
+
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int first_tile = wc0 < wc1 ? c_tile : -1;
+    float best_v = 0.f;
+    int best_i = -1;
+
+    auto emit = [&](int tile, const float (&v)[4]) {
+        if (c != 0) return;   // token 0 sits in MMA column 0 (lanes c == 0)
+        const int r0 = row0 + tile * 16 + g, r1 = r0 + 8;
+        float a = v[0], b = v[2];
+        if (!GROUP && rs != nullptr) {
+            a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
+            b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
+        }
+        if (p.y != nullptr) {
+            if (p.y_f32) {
+                if (r0 < row1) static_cast<float*>(p.y)[r0] = a;
+                if (r1 < row1) static_cast<float*>(p.y)[r1] = b;
+            } else {
+                if (r0 < row1) static_cast<__half*>(p.y)[r0] = __float2half_rn(a);
+                if (r1 < row1) static_cast<__half*>(p.y)[r1] = __float2half_rn(b);
+            }
+        }
+        if (p.arg_out != nullptr) {
+            const int lim = min(row1, p.arg_limit);
+            if (r0 < lim && argmax_better(a, r0, best_v, best_i)) { best_v = a; best_i = r0; }
+            if (r1 < lim && argmax_better(b, r1, best_v, best_i)) { best_v = b; best_i = r1; }
+        }
+    };
+
+    int seg_lo = wc0;
+#pragma unroll 1
+    for (int j = wc0; j < wc1; ++j) {
+        cp_async_wait<kS - 1>();
+        const unsigned char* sl = my_ring_p + c_slot * kSlot;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        uint4 wg[2], wh[2];
+        wg[0] = v0 ? *reinterpret_cast<const uint4*>(sl) : z;
+        wg[1] = v0 ? *reinterpret_cast<const uint4*>(sl + 512) : z;
+        wh[0] = v1 ? *reinterpret_cast<const uint4*>(sl + 1024) : z;
+        wh[1] = v1 ? *reinterpret_cast<const uint4*>(sl + 1536) : z;
+        const __half* xp_ = my_x + (c_kc << 7);
+        uint4 xv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) xv[u] = *reinterpret_cast<const uint4*>(xp_ + u * 8);
+        float s0 = 1.f, s1 = 1.f;
+        if (GROUP) {
+            s0 = half_bits_to_float(sp0[c_kc]);
+            s1 = half_bits_to_float(sp1[c_kc]);
+        }
+        issue();   // this slot's bytes are in registers: refill it
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        // lane (g, c): bytes 4t..4t+3 of its 32 row bytes are MMA k-step t
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint32_t b0 = u4w(wg[t >> 2], t & 3), b1 = u4w(wh[t >> 2], t & 3);
+            float e[4] = {0.f, 0.f, 0.f, 0.f};
+            mma16816(e, e4m3x2_lo(b0), e4m3x2_lo(b1), e4m3x2_hi(b0), e4m3x2_hi(b1), u4w(xv[t >> 1], (t & 1) * 2),
+                     u4w(xv[t >> 1], (t & 1) * 2 + 1));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) d[k] += e[k];
+        }
+        acc[0] = fmaf(s0, d[0], acc[0]);
+        acc[1] = fmaf(s0, d[1], acc[1]);
+        acc[2] = fmaf(s1, d[2], acc[2]);
+        acc[3] = fmaf(s1, d[3], acc[3]);
+        if (++c_slot == kS) c_slot = 0;
+        const bool tile_done = ++c_kc == cpt;
+        if (j + 1 == wc1 || tile_done) {
+            if (seg_lo == c_tile * cpt && j + 1 == (c_tile + 1) * cpt) {
+                emit(c_tile, acc);
+            } else {
+                float* dst = wslots + ((size_t)(warp * 2 + (c_tile == first_tile ? 0 : 1)) * 32 + lane) * 4;
+                *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            }
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            seg_lo = j + 1;
+        }
+        if (tile_done) {
+            c_kc = 0;
+            ++c_tile;
+            c_rows();
+        }
+    }
+    cp_async_wait<0>();
+    TRACE(3);
+    __syncthreads();
+    TRACE(4);
+
+    for (int t = warp; t < T; t += kWarps) {
+        const int wa_ = (int)owner_of((long long)t * cpt, L, We);
+        const int wb_ = (int)owner_of((long long)(t + 1) * cpt - 1, L, We);
+        if (wa_ == wb_) continue;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w = wa_; w <= wb_; ++w) {
+            const int w0 = (int)((long long)w * L / We);
+            const int slot = (t == w0 / cpt) ? 0 : 1;
+            const float4 f = *reinterpret_cast<const float4*>(wslots + ((size_t)(w * 2 + slot) * 32 + lane) * 4);
+            v[0] += f.x;
+            v[1] += f.y;
+            v[2] += f.z;
+            v[3] += f.w;
+        }
+        emit(t, v);
+    }
+    TRACE(5);
+
+    if (p.arg_out != nullptr) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (argmax_better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+        }
+        if (lane == 0) {
+            s_red[warp] = best_v;
+            s_redi[warp] = best_i;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            best_v = lane < kWarps ? s_red[lane] : 0.f;
+            best_i = lane < kWarps ? s_redi[lane] : -1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+                if (argmax_better(ov, oi, best_v, best_i)) { best_v = ov; best_i = oi; }
+            }
+            int last = 0;
+            if (lane == 0) {
+                __stcg(p.arg_val + cta, best_v);
+                __stcg(p.arg_idx + cta, best_i);
+                __threadfence();
+                last = (atomicAdd(p.arg_done, 1) == G - 1);
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                float bv = 0.f;
+                int bi = -1;
+                for (int i = lane; i < G; i += 32) {
+                    const float v = ldcg_f32(p.arg_val + i);
+                    const int ix = ldcg_s32(p.arg_idx + i);
+                    if (argmax_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+                    __stcg(p.arg_val + i, 0.f);   // leave the workspace all-zero
+                    __stcg(p.arg_idx + i, 0);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (argmax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                }
+                if (lane == 0) {
+                    *p.arg_out = bi;
+                    *p.arg_done = 0;
+                }
+            }
+        }
+    }
+}
+
 // Any alignment, any K: one warp per (row, token), scalar decode.  Used when a
 // pointer or K does not meet the streaming kernel's 16-byte layout rules.
 __device__ __forceinline__ uint16_t ld_u16_bytes(const void* base, size_t byte_off) {
@@ -541,12 +916,22 @@ Plan make_plan(int nt, int N, int K, int wk, int sms, bool argmax) {
     return pl;
 }
 
+// AF_M1_KERNEL=0 routes one-token FP8 GEMVs through the general kernel (for A/B runs).
+bool m1_enabled() {
+    static bool v = [] {
+        const char* e = getenv("AF_M1_KERNEL");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 constexpr int kWarpsPerCta = 16;
 constexpr int kRingSlots = 10;   // chunk slots per warp (1 KB each)
+constexpr int kM1Warps = 8;      // warps per CTA of the one-token FP8 kernel (2 CTAs per SM)
 
-template <int WK, int NT>
+template <int WK, int NT, bool SX>
 cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    auto kern = gemv_stream_kernel<WK, NT, kWarpsPerCta, kRingSlots>;
+    auto kern = gemv_stream_kernel<WK, NT, kWarpsPerCta, kRingSlots, SX>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -562,15 +947,37 @@ cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cu
     return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
-cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
+template <bool GROUP, int NS>
+cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
+    auto kern = gemv_fp8_m1_kernel<GROUP, kM1Warps, NS>;
+    static std::once_flag flags[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(flags[dev % kMaxDevices], [&] {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax - 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared);
+        attr_err[dev % kMaxDevices] = e;
+    });
+    if (attr_err[dev % kMaxDevices] != cudaSuccess) return attr_err[dev % kMaxDevices];
+    return launch_pdl(kern, dim3(pl.grid), dim3(kM1Warps * 32), smem, st, prm);
+}
+
+cudaError_t dispatch(int wk, bool sx, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
     const bool two = pl.nt == 2;
     switch (wk) {
         case W_FP8_GROUP:
-            return two ? launch_stream<W_FP8_GROUP, 2>(prm, pl, smem, st) : launch_stream<W_FP8_GROUP, 1>(prm, pl, smem, st);
+            if (sx) return launch_stream<W_FP8_GROUP, 1, true>(prm, pl, smem, st);
+            return two ? launch_stream<W_FP8_GROUP, 2, false>(prm, pl, smem, st)
+                       : launch_stream<W_FP8_GROUP, 1, false>(prm, pl, smem, st);
         case W_FP8_ROW:
-            return two ? launch_stream<W_FP8_ROW, 2>(prm, pl, smem, st) : launch_stream<W_FP8_ROW, 1>(prm, pl, smem, st);
+            if (sx) return launch_stream<W_FP8_ROW, 1, true>(prm, pl, smem, st);
+            return two ? launch_stream<W_FP8_ROW, 2, false>(prm, pl, smem, st)
+                       : launch_stream<W_FP8_ROW, 1, false>(prm, pl, smem, st);
         default:
-            return two ? launch_stream<W_F16, 2>(prm, pl, smem, st) : launch_stream<W_F16, 1>(prm, pl, smem, st);
+            return two ? launch_stream<W_F16, 2, false>(prm, pl, smem, st) : launch_stream<W_F16, 1, false>(prm, pl, smem, st);
     }
 }
 
@@ -633,12 +1040,45 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         sc = round_up(rows * (K / 128) * 2 + 32, 128);
         if (ring + slots + sc > budget || sc > 32 * 1024) sc = 0;
     }
-    size_t xs = round_up((size_t)M * (K + kXsPad) * sizeof(__half), 128);
-    if (ring + slots + sc + xs > budget) xs = 0;
-    prm.xs_stride = xs ? K + kXsPad : 0;
+    // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
+    // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
+    if (wk != W_F16 && M == 1 && K % 128 == 0 && aligned(x, 16) && m1_enabled()) {
+        const size_t cap = 113 * 1024;
+        const size_t slots1 = (size_t)kM1Warps * 2 * 32 * 4 * sizeof(float);
+        const size_t xs1 = round_up((size_t)K * 2, 128);
+        const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
+        for (int ns : {5, 3}) {
+            const size_t ring1 = (size_t)kM1Warps * ns * 2048;
+            for (size_t scx : {sc1, (size_t)0}) {
+                if (ring1 + slots1 + xs1 + scx > cap) continue;
+                prm.xs_stride = 0;
+                prm.xs_bytes = (int)xs1;
+                prm.sc_bytes = (int)scx;
+                const size_t smem1 = ring1 + xs1 + scx + slots1;
+                cudaError_t e = (wk == W_FP8_GROUP)
+                                    ? (ns == 5 ? launch_m1<true, 5>(prm, pl, smem1, st) : launch_m1<true, 3>(prm, pl, smem1, st))
+                                    : (ns == 5 ? launch_m1<false, 5>(prm, pl, smem1, st) : launch_m1<false, 3>(prm, pl, smem1, st));
+                return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_fp8_m1_kernel");
+            }
+        }
+    }
+    // Order of sacrifice when shared memory runs short: staged scales (read
+    // from L2 instead), then the split path (FP16 operands instead), then
+    // staged x (read from L2 instead).
+    bool sx = false;   // one-token FP8 cases not taken above use FP16 operands
+    size_t stride = round_up((size_t)K, 128) + 64;
+    size_t xs = round_up(4 * stride, 128);
+    if (sx && ring + slots + sc + xs > budget) sc = 0;
+    if (sx && ring + slots + sc + xs > budget) sx = false;
+    if (!sx) {
+        stride = (size_t)K + kXsPad;
+        xs = round_up((size_t)M * stride * sizeof(__half), 128);
+        if (ring + slots + sc + xs > budget) xs = 0;
+    }
+    prm.xs_stride = xs ? (int)stride : 0;
     prm.xs_bytes = (int)xs;
     prm.sc_bytes = (int)sc;
-    cudaError_t e = dispatch(wk, prm, pl, ring + xs + sc + slots, st);
+    cudaError_t e = dispatch(wk, sx, prm, pl, ring + xs + sc + slots, st);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_stream_kernel");
 }
 

@@ -71,16 +71,6 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// D = A(16x32 e4m3, row) * B(32x8 e5m2, col) + C, FP32 accumulate.
-__device__ __forceinline__ void mma16832_e4m3_e5m2(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                                   uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e5m2.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // Programmatic dependent launch: let the next kernel of the stream start its
 // independent prologue (weight prefetch) now, and block until the previous
 // kernel's memory is visible before touching anything it may have written.

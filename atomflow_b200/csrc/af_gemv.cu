@@ -93,7 +93,7 @@ __device__ __forceinline__ long long owner_of(long long c, long long n, long lon
     return ((c + 1) * parts - 1) / n;
 }
 
-template <int WK, int NT, int kWarps, int kS, bool SX>
+template <int WK, int NT, int kWarps, int kS>
 __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int POS = (WK == W_F16) ? 32 : 64;   // positions per chunk
@@ -187,57 +187,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     pdl_wait();
     TRACE(1);
 
-    // SX (one token, FP8 weights): x is re-expressed as four E5M2 pieces in a
-    // common power-of-two scale, x * 2^xe = p0 + p1 + p2 + p3 -- exact for
-    // every FP16 value down to 2^-16 of the largest |x| (4 x 3 significant bits
-    // cover FP16's 11) -- so the FP8 weights feed the tensor cores directly
-    // (e4m3 x e5m2 MMA, FP32 accumulate) with no per-weight conversion.  Piece
-    // q of x lives in row q of xs (stride xs_stride bytes).
-    __shared__ int s_xe;
-    unsigned char* xp = reinterpret_cast<unsigned char*>(xs);
-    if (SX) {
-        float m = 0.f;
-        for (int k = threadIdx.x * 8; k < p.K; k += kThreads * 8) {
-            const uint4 v = ldcg_u4(p.x + k);
-            const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float2 f = __half22float2(h[u]);
-                m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_best_v[warp] = m;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float mm = 0.f;
-            for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, s_best_v[w]);
-            int e = 0;
-            if (mm > 0.f) frexpf(mm, &e);   // mm < 2^e
-            s_xe = 15 - e;                   // max |x| * 2^xe < 2^15 <= E5M2 max
-        }
-        __syncthreads();
-        const int xe = s_xe;
-        for (int k = threadIdx.x * 8; k < p.K; k += kThreads * 8) {
-            const uint4 v = ldcg_u4(p.x + k);
-            const __half* h = reinterpret_cast<const __half*>(&v);
-            uint32_t pk[4][2] = {};
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                float r = ldexpf(__half2float(h[u]), xe);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(r, __NV_SATFINITE, __NV_E5M2);
-                    r -= __half2float(__half(__nv_cvt_fp8_to_halfraw(b, __NV_E5M2)));
-                    pk[q][u >> 2] |= (uint32_t)b << (8 * (u & 3));
-                }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                *reinterpret_cast<uint2*>(xp + (size_t)q * p.xs_stride + k) = make_uint2(pk[q][0], pk[q][1]);
-        }
-    } else if (p.xs_stride > 0) {
+    if (p.xs_stride > 0) {
         const int k8 = p.K >> 3;
         const int total = p.M * k8;
         for (int i = threadIdx.x; i < total; i += kThreads) {
@@ -299,25 +249,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int k = 0; k < 4; ++k) d[nt][k] = 0.f;
-        if (SX) {
-            // lane (g, c) supplies MMA column g = x piece g (columns 4..7 are zero)
-            const uint4 xb = g < 4 ? *reinterpret_cast<const uint4*>(xp + (size_t)g * p.xs_stride + pos)
-                                   : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                float e[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16832_e4m3_e5m2(e, u4w(w0, 2 * t), u4w(w1, 2 * t), u4w(w0, 2 * t + 1), u4w(w1, 2 * t + 1),
-                                   u4w(xb, 2 * t), u4w(xb, 2 * t + 1));
-#pragma unroll
-                for (int k = 0; k < 4; ++k) d[0][k] += e[k];
-            }
-        }
         uint32_t xf[NT][LPOS / 2];
-        if (!SX) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
-        }
-        constexpr int KSTEPS = SX ? 0 : (WK == W_F16) ? 2 : 4;
+        for (int nt = 0; nt < NT; ++nt) load_x(min(nt * 8 + g, p.M - 1), pos, xf[nt]);
+        constexpr int KSTEPS = (WK == W_F16) ? 2 : 4;
 #pragma unroll
         for (int t = 0; t < KSTEPS; ++t) {
             uint32_t a0, a1, a2, a3;
@@ -367,17 +302,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     auto emit = [&](int tile, float (&v)[NT][4]) {
         const int r0 = row0 + tile * 16 + g;
         const int r1 = r0 + 8;
-        if (SX) {
-            // columns 0..3 hold the four pieces' sums: lanes c = 0 and 1 each
-            // own two; the total lands in lane c = 0 (token 0), unscaled by 2^-xe
-            float a = v[0][0] + v[0][1], b = v[0][2] + v[0][3];
-            a += __shfl_down_sync(0xffffffffu, a, 1);
-            b += __shfl_down_sync(0xffffffffu, b, 1);
-            const int xe = s_xe;
-            v[0][0] = ldexpf(a, -xe);
-            v[0][2] = ldexpf(b, -xe);
-            v[0][1] = v[0][3] = 0.f;
-        }
         if (WK == W_FP8_ROW && p.s != nullptr) {
             const float* s32 = static_cast<const float*>(p.s);
             const float s0 = r0 < row1 ? __ldg(s32 + r0) : 0.f;
@@ -929,9 +853,9 @@ constexpr int kWarpsPerCta = 16;
 constexpr int kRingSlots = 10;   // chunk slots per warp (1 KB each)
 constexpr int kM1Warps = 8;      // warps per CTA of the one-token FP8 kernel (2 CTAs per SM)
 
-template <int WK, int NT, bool SX>
+template <int WK, int NT>
 cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    auto kern = gemv_stream_kernel<WK, NT, kWarpsPerCta, kRingSlots, SX>;
+    auto kern = gemv_stream_kernel<WK, NT, kWarpsPerCta, kRingSlots>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -965,19 +889,15 @@ cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaSt
     return launch_pdl(kern, dim3(pl.grid), dim3(kM1Warps * 32), smem, st, prm);
 }
 
-cudaError_t dispatch(int wk, bool sx, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
+cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
     const bool two = pl.nt == 2;
     switch (wk) {
         case W_FP8_GROUP:
-            if (sx) return launch_stream<W_FP8_GROUP, 1, true>(prm, pl, smem, st);
-            return two ? launch_stream<W_FP8_GROUP, 2, false>(prm, pl, smem, st)
-                       : launch_stream<W_FP8_GROUP, 1, false>(prm, pl, smem, st);
+            return two ? launch_stream<W_FP8_GROUP, 2>(prm, pl, smem, st) : launch_stream<W_FP8_GROUP, 1>(prm, pl, smem, st);
         case W_FP8_ROW:
-            if (sx) return launch_stream<W_FP8_ROW, 1, true>(prm, pl, smem, st);
-            return two ? launch_stream<W_FP8_ROW, 2, false>(prm, pl, smem, st)
-                       : launch_stream<W_FP8_ROW, 1, false>(prm, pl, smem, st);
+            return two ? launch_stream<W_FP8_ROW, 2>(prm, pl, smem, st) : launch_stream<W_FP8_ROW, 1>(prm, pl, smem, st);
         default:
-            return two ? launch_stream<W_F16, 2, false>(prm, pl, smem, st) : launch_stream<W_F16, 1, false>(prm, pl, smem, st);
+            return two ? launch_stream<W_F16, 2>(prm, pl, smem, st) : launch_stream<W_F16, 1>(prm, pl, smem, st);
     }
 }
 
@@ -1062,23 +982,14 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
             }
         }
     }
-    // Order of sacrifice when shared memory runs short: staged scales (read
-    // from L2 instead), then the split path (FP16 operands instead), then
-    // staged x (read from L2 instead).
-    bool sx = false;   // one-token FP8 cases not taken above use FP16 operands
-    size_t stride = round_up((size_t)K, 128) + 64;
-    size_t xs = round_up(4 * stride, 128);
-    if (sx && ring + slots + sc + xs > budget) sc = 0;
-    if (sx && ring + slots + sc + xs > budget) sx = false;
-    if (!sx) {
-        stride = (size_t)K + kXsPad;
-        xs = round_up((size_t)M * stride * sizeof(__half), 128);
-        if (ring + slots + sc + xs > budget) xs = 0;
-    }
+    const size_t stride = (size_t)K + kXsPad;
+    size_t xs = round_up((size_t)M * stride * sizeof(__half), 128);
+    if (ring + slots + sc + xs > budget) sc = 0;   // scales from L2 before giving up staged x
+    if (ring + slots + sc + xs > budget) xs = 0;   // then x from L2
     prm.xs_stride = xs ? (int)stride : 0;
     prm.xs_bytes = (int)xs;
     prm.sc_bytes = (int)sc;
-    cudaError_t e = dispatch(wk, sx, prm, pl, ring + xs + sc + slots, st);
+    cudaError_t e = dispatch(wk, prm, pl, ring + xs + sc + slots, st);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_stream_kernel");
 }
 

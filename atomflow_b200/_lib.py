@@ -58,6 +58,7 @@ C_SYMBOLS = {
     "af_lm_head_gemv": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _vp, _i, _vp, _sz, _vp]),
     "af_argmax_workspace_bytes": (_sz, [_i]),
     "af_argmax_f32": (_i, [_vp, _i, _vp, _i, _vp, _sz, _vp]),
+    "af_argmax_f32_noalloc": (_i, [_vp, _i, _vp, _i, _vp]),
     "af_view_last_status": (_i, []),
 }
 # C++ launchers with the reference's signatures (include/ops/kernel.h); references are pointers.

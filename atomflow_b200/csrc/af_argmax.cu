@@ -196,3 +196,82 @@ extern "C" af_status af_argmax_f32(const float* logits, int V, int* d_out, af_ar
                                static_cast<cudaStream_t>(stream), logits, n, d_out, ws);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "argmax_kernel");
 }
+
+// ------------------------------------------------------ no-allocation argmax ---
+//
+// Some callers cannot allocate device memory at all -- code that runs where
+// cudaMalloc is forbidden or unavailable (a host that owns every allocation
+// and hands out only input/output buffers, or an allocator-free deployment) --
+// and so cannot provide the workspace af_argmax_f32 needs.  For them the same
+// kernel runs on a scratch block that lives inside this library image: a
+// file-scope __device__ array of kNoAllocScratchBytes, present on every GPU
+// that loads the library until the process exits.
+//
+// The array's name in host code is only a host-side handle, not a device
+// address; the device address is looked up with cudaGetSymbolAddress, once per
+// device with that device current, on the first call made on that device.
+// That first call should therefore come before any stream capture.  All calls
+// share the one array: calls that can overlap on the GPU (different streams
+// without ordering between them) race on it.
+
+namespace af {
+constexpr int kNoAllocBlocks = 256;                 // candidate slots in the scratch
+constexpr int kNoAllocMaxV = 1 << 28;               // largest V accepted
+constexpr size_t kNoAllocScratchBytes = 256 + 2 * kNoAllocBlocks * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+unsigned char* noalloc_scratch_ptr(af_status* st) {
+    static std::once_flag flags[kMaxDevices];
+    static unsigned char* ptrs[kMaxDevices] = {nullptr};
+    static cudaError_t errs[kMaxDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *st = cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidDevice, "af_argmax_f32_noalloc: device");
+        return nullptr;
+    }
+    std::call_once(flags[dev], [&] {
+        void* p = nullptr;
+        errs[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        ptrs[dev] = static_cast<unsigned char*>(p);
+    });
+    if (errs[dev] != cudaSuccess || ptrs[dev] == nullptr) {
+        *st = cuda_fail(errs[dev] != cudaSuccess ? errs[dev] : cudaErrorInvalidSymbol,
+                        "af_argmax_f32_noalloc: cudaGetSymbolAddress");
+        return nullptr;
+    }
+    *st = AF_OK;
+    return ptrs[dev];
+}
+}  // namespace
+}  // namespace af
+
+extern "C" af_status af_argmax_f32_noalloc(const float* logits, int V, int* d_out, af_argmax_mode mode,
+                                           void* stream) {
+    if (V <= 0 || logits == nullptr || d_out == nullptr) return AF_ERR_INVALID;
+    if (mode != AF_ARGMAX_TRUE && mode != AF_ARGMAX_REF_COMPAT) return AF_ERR_INVALID;
+    if (V > kNoAllocMaxV) {
+        snprintf(g_cuda_err, sizeof(g_cuda_err),
+                 "af_argmax_f32_noalloc: V = %d exceeds the built-in scratch limit of %d logits", V,
+                 kNoAllocMaxV);
+        return AF_ERR_UNSUPPORTED;
+    }
+    const int sms = device_sm_count();
+    if (sms <= 0) return AF_ERR_CUDA;
+    af_status st = AF_OK;
+    unsigned char* b = noalloc_scratch_ptr(&st);
+    if (b == nullptr) return st;
+    const int n = (mode == AF_ARGMAX_REF_COMPAT && V > 65536) ? 65536 : V;
+    int blocks = argmax_blocks(n, sms);
+    if (blocks > kNoAllocBlocks) blocks = kNoAllocBlocks;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The arrival counter must start at zero; the kernel leaves it (and the
+    // candidates) zeroed, but clear it anyway in case an earlier call was cut short.
+    cudaError_t e = cudaMemsetAsync(b, 0, 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "af_argmax_f32_noalloc: clear");
+    ArgmaxWs ws{reinterpret_cast<int*>(b), reinterpret_cast<float*>(b + 256),
+                reinterpret_cast<int*>(b + 256 + kNoAllocBlocks * 4)};
+    e = launch_pdl(argmax_kernel, dim3(blocks), dim3(kArgThreads), 0, s, logits, n, d_out, ws);
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "af_argmax_f32_noalloc: launch");
+}

@@ -98,6 +98,18 @@ size_t af_argmax_workspace_bytes(int V);
 af_status af_argmax_f32(const float* logits, int V, int* d_out, af_argmax_mode mode,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ----------------------------------------------- argmax, no allocation ---
+ * No counterpart in the reference.  The same argmax as af_argmax_f32 for
+ * callers that cannot allocate device memory (no cudaMalloc available or
+ * allowed, so no workspace to pass): its scratch is a fixed ~2.3 KB block
+ * inside the library, resident on every GPU that loads it until exit.
+ *   - V above 268,435,456 (1 << 28) returns AF_ERR_UNSUPPORTED, launching nothing.
+ *   - The first call on a device looks up that block's device address; make it
+ *     before any stream capture.
+ *   - All calls share the block: calls that may overlap on the GPU race.
+ * It allocates nothing and calls no allocating routine. */
+af_status af_argmax_f32_noalloc(const float* logits, int V, int* d_out, af_argmax_mode mode, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,7 +40,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 from atomflow_b200 import lib as af_lib  # noqa: E402
-from atomflow_b200.quant import quantize_gs128, quantize_row  # noqa: E402
+from atomflow_b200.quant import quantize_gs128  # noqa: E402
+from atomflow_b200.tp import shard  # noqa: E402
 
 D, FFN, QKV = 3072, 8192, 5120
 NLAYERS = 28
@@ -131,11 +132,7 @@ def make_layerset(device, rank, world, seed=1234):
             g.manual_seed(seed + 1000 * layer + pi)
             w = torch.randn(N, K, generator=g, device=device, dtype=torch.float32) * 0.02
             x = torch.randn(1, K, generator=g, device=device, dtype=torch.float32).half()
-            if world > 1 and split == "col":
-                w = w.chunk(world, 0)[rank]
-            elif world > 1:
-                w = w.chunk(world, 1)[rank]
-                x = x.chunk(world, 1)[rank]
+            w, x = shard(w, x, split, rank, world)
             q, s = quantize_gs128(w.contiguous())
             del w
             items.append(dict(name=name, layer=layer, N=q.shape[0], K=q.shape[1], split=split,
@@ -288,8 +285,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist_on = world > 1
-    if args.impl == "reference" and dist_on and rank != 0:
+    dist_on = world > 1 and args.impl == "ours"
+    if args.impl == "reference" and world > 1 and rank != 0:
         return 0                     # the reference arm runs on rank 0 alone
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -383,8 +380,7 @@ def main():
         sampler.stop()
 
     if rank != 0:
-        torch.distributed.destroy_process_group()
-        return 0
+        finish(dist_on)
 
     peak, peak_kind = measured_peaks()
     per_rank_gbs = step_bytes / (ms_step / 1e3) / 1e9
@@ -417,9 +413,20 @@ def main():
                                          "w8a16_gemv_kernel, compiled from its sources), run on this GPU"}
         out["reference_kernel_launches"] = launches
     print(json.dumps(out))
+    finish(dist_on)
+
+
+def finish(dist_on):
+    """Leave without tearing NCCL down: graphs that captured NCCL collectives are
+    still alive, and destroying the communicator under them can block.  All
+    ranks meet at a barrier first, so no rank exits with work in flight."""
+    torch.cuda.synchronize()
     if dist_on:
-        torch.distributed.destroy_process_group()
-    return 0
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def traffic_from_profiles(workload, launches_per_step):

@@ -72,6 +72,7 @@ struct GemvParams {
     int* arg_idx;         // [CTAs]
     int* arg_done;        // [1]
     int arg_limit;        // rows >= arg_limit are not argmax candidates
+    int pre;              // one-token kernel: ring slots requested before griddepcontrol.wait
 };
 
 __device__ __forceinline__ uint32_t u4w(const uint4& v, int t) {
@@ -470,15 +471,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 // (every launch_w8a16_gemv of engine.cu, and an FP8 lm_head).  Same row split
 // and warp ranges as gemv_stream_kernel, tuned for a chain of dependent GEMVs:
 //   * a chunk is a whole 128-wide scale group (a lane streams 32 B of rows g
-//     and g+8), all per-tile addressing is hoisted out of the chunk loop;
+//     and g+8: bytes [16c, 16c+16) and [64+16c, 64+16c+16), so that each load
+//     instruction covers whole 32-byte sectors), all per-tile addressing is
+//     hoisted out of the chunk loop;
 //   * 8 warps and <= 113 KB of shared memory per CTA, so that the CTA of the
 //     NEXT GEMV of the stream sits on the same SM and fills its own ring
 //     (cp.async, before its griddepcontrol.wait) while this one computes --
 //     the SM's memory pipe never idles between kernels;
 //   * x arrives by one bulk copy on the TMA engine straight into shared memory,
 //     so it does not queue behind the co-resident CTA's weight requests.
-template <bool GROUP, int kWarps, int kS>
-__global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvParams p) {
+template <bool GROUP, int kWarps, int kS, int kMinCtas>
+__global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
 #ifdef AF_EXP_TRACE
@@ -535,21 +538,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvP
     const uint8_t* i_p1 = nullptr;
     auto i_rows = [&]() {
         const int r0 = row0 + i_tile * 16 + g;
-        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K + c * 32 : nullptr;
-        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K + c * 32 : nullptr;
+        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K + c * 16 : nullptr;
+        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K + c * 16 : nullptr;
     };
     i_rows();
     auto issue = [&]() {
         if (i_left > 0) {
             const uint32_t d = my_ring + i_slot * kSlot;
             const int off = i_kc << 7;
+            // lanes c = 0..3 of a row cover 64 contiguous bytes per instruction
             if (i_p0) {
                 cp_async16(d, i_p0 + off);
-                cp_async16(d + 512, i_p0 + off + 16);
+                cp_async16(d + 512, i_p0 + off + 64);
             }
             if (i_p1) {
                 cp_async16(d + 1024, i_p1 + off);
-                cp_async16(d + 1536, i_p1 + off + 16);
+                cp_async16(d + 1536, i_p1 + off + 64);
             }
             --i_left;
             if (++i_slot == kS) i_slot = 0;
@@ -561,8 +565,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvP
         }
         cp_async_commit();
     };
+    // Only part of the ring is requested before griddepcontrol.wait (p.pre slots);
+    // the rest after x has landed, so that the previous kernel's x/y traffic and
+    // our own x fetch do not wait behind a full prefetch.
 #pragma unroll 1
-    for (int q = 0; q < kS; ++q) issue();
+    for (int q = 0; q < p.pre; ++q) issue();
 
     pdl_wait();
     TRACE(1);
@@ -571,14 +578,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvP
         mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.K * 2u);
         bulk_g2s(smem_u32(xs), p.x, (uint32_t)p.K * 2u, smem_u32(&s_xbar));
     }
-    cp_async_wait<kS>();   // the scale group (the oldest) has landed
+    cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
     mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
+#pragma unroll 1
+    for (int q = p.pre; q < kS; ++q) issue();
     TRACE(2);
 
     // ---- compute cursor ----
     const unsigned char* my_ring_p = ring + (size_t)warp * kS * kSlot + lane * 16;
-    const __half* my_x = xs + c * 32;
+    const __half* my_x = xs + c * 16;
     const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
     const float* rs = static_cast<const float*>(p.s);
     int c_tile = wc0 / (cpt > 0 ? cpt : 1);
@@ -643,10 +652,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvP
         wg[1] = v0 ? *reinterpret_cast<const uint4*>(sl + 512) : z;
         wh[0] = v1 ? *reinterpret_cast<const uint4*>(sl + 1024) : z;
         wh[1] = v1 ? *reinterpret_cast<const uint4*>(sl + 1536) : z;
+        // the lane's 32 positions: [16c, 16c+16) and [64+16c, 64+16c+16) of the chunk
         const __half* xp_ = my_x + (c_kc << 7);
         uint4 xv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) xv[u] = *reinterpret_cast<const uint4*>(xp_ + u * 8);
+        xv[0] = *reinterpret_cast<const uint4*>(xp_);
+        xv[1] = *reinterpret_cast<const uint4*>(xp_ + 8);
+        xv[2] = *reinterpret_cast<const uint4*>(xp_ + 64);
+        xv[3] = *reinterpret_cast<const uint4*>(xp_ + 72);
         float s0 = 1.f, s1 = 1.f;
         if (GROUP) {
             s0 = half_bits_to_float(sp0[c_kc]);
@@ -654,7 +666,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_fp8_m1_kernel(const GemvP
         }
         issue();   // this slot's bytes are in registers: refill it
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        // lane (g, c): bytes 4t..4t+3 of its 32 row bytes are MMA k-step t
+        // lane (g, c): bytes 4t..4t+3 of its 32 row bytes are MMA k-step t; its
+        // x halves are in the same order, so the permutation of k cancels
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             const uint32_t b0 = u4w(wg[t >> 2], t & 3), b1 = u4w(wh[t >> 2], t & 3);
@@ -840,6 +853,25 @@ Plan make_plan(int nt, int N, int K, int wk, int sms, bool argmax) {
     return pl;
 }
 
+// AF_M1_VARIANT=0..2 selects the one-token kernel's shape (tuning runs).
+int m1_variant() {
+    static int v = [] {
+        const char* e = getenv("AF_M1_VARIANT");
+        int k = e ? atoi(e) : 0;
+        return (k >= 0 && k <= 5) ? k : 0;
+    }();
+    return v;
+}
+
+// AF_M1_PRE=n: ring slots requested before griddepcontrol.wait (tuning; default all).
+int m1_pre(int ns) {
+    static int v = [] {
+        const char* e = getenv("AF_M1_PRE");
+        return e ? atoi(e) : -1;
+    }();
+    return (v < 0 || v > ns) ? ns : v;
+}
+
 // AF_M1_KERNEL=0 routes one-token FP8 GEMVs through the general kernel (for A/B runs).
 bool m1_enabled() {
     static bool v = [] {
@@ -871,9 +903,10 @@ cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cu
     return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
-template <bool GROUP, int NS>
+template <bool GROUP, int NW, int NS>
 cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
-    auto kern = gemv_fp8_m1_kernel<GROUP, kM1Warps, NS>;
+    // a ring past ~100 KB means one CTA per SM: registers may grow
+    auto kern = gemv_fp8_m1_kernel<GROUP, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2)>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -886,7 +919,7 @@ cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaSt
         attr_err[dev % kMaxDevices] = e;
     });
     if (attr_err[dev % kMaxDevices] != cudaSuccess) return attr_err[dev % kMaxDevices];
-    return launch_pdl(kern, dim3(pl.grid), dim3(kM1Warps * 32), smem, st, prm);
+    return launch_pdl(kern, dim3(pl.grid), dim3(NW * 32), smem, st, prm);
 }
 
 cudaError_t dispatch(int wk, const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
@@ -963,21 +996,35 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
     // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
     if (wk != W_F16 && M == 1 && K % 128 == 0 && aligned(x, 16) && m1_enabled()) {
-        const size_t cap = 113 * 1024;
-        const size_t slots1 = (size_t)kM1Warps * 2 * 32 * 4 * sizeof(float);
+        // (warps, ring slots) options, most in-flight bytes first; two CTAs per SM.
+        struct Cfg { int nw, ns; };
+        const int var = m1_variant();
+        const Cfg cfgs[6][2] = {{{8, 5}, {8, 3}}, {{16, 3}, {16, 2}}, {{12, 4}, {12, 2}}, {{6, 5}, {6, 3}},
+                                {{8, 12}, {8, 8}}, {{16, 6}, {16, 4}}};
         const size_t xs1 = round_up((size_t)K * 2, 128);
         const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
-        for (int ns : {5, 3}) {
-            const size_t ring1 = (size_t)kM1Warps * ns * 2048;
+        for (const Cfg& cf : cfgs[var]) {
+            const bool deep = cf.nw * cf.ns * 2 > 100;
+            const size_t cap = deep ? kSmemMax - 1024 : (cf.nw <= 6 ? 75 : 113) * 1024;   // 1, 3 or 2 CTAs per SM
+            const size_t slots1 = (size_t)cf.nw * 2 * 32 * 4 * sizeof(float);
+            const size_t ring1 = (size_t)cf.nw * cf.ns * 2048;
             for (size_t scx : {sc1, (size_t)0}) {
                 if (ring1 + slots1 + xs1 + scx > cap) continue;
                 prm.xs_stride = 0;
+                prm.pre = m1_pre(cf.ns);
                 prm.xs_bytes = (int)xs1;
                 prm.sc_bytes = (int)scx;
                 const size_t smem1 = ring1 + xs1 + scx + slots1;
-                cudaError_t e = (wk == W_FP8_GROUP)
-                                    ? (ns == 5 ? launch_m1<true, 5>(prm, pl, smem1, st) : launch_m1<true, 3>(prm, pl, smem1, st))
-                                    : (ns == 5 ? launch_m1<false, 5>(prm, pl, smem1, st) : launch_m1<false, 3>(prm, pl, smem1, st));
+                cudaError_t e;
+                const bool grp = wk == W_FP8_GROUP;
+#define AF_M1(NW, NS) (grp ? launch_m1<true, NW, NS>(prm, pl, smem1, st) : launch_m1<false, NW, NS>(prm, pl, smem1, st))
+                if (cf.nw == 8 && cf.ns <= 5) e = cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
+                else if (cf.nw == 16 && cf.ns <= 3) e = cf.ns == 3 ? AF_M1(16, 3) : AF_M1(16, 2);
+                else if (cf.nw == 12) e = cf.ns == 4 ? AF_M1(12, 4) : AF_M1(12, 2);
+                else if (cf.nw == 6) e = cf.ns == 5 ? AF_M1(6, 5) : AF_M1(6, 3);
+                else if (cf.nw == 8) e = cf.ns == 12 ? AF_M1(8, 12) : AF_M1(8, 8);
+                else e = cf.ns == 6 ? AF_M1(16, 6) : AF_M1(16, 4);
+#undef AF_M1
                 return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_fp8_m1_kernel");
             }
         }

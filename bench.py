@@ -40,7 +40,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 from atomflow_b200 import lib as af_lib  # noqa: E402
-from atomflow_b200.quant import quantize_gs128  # noqa: E402
+from atomflow_b200.quant import quantize_gs128, quantize_row  # noqa: E402
 from atomflow_b200.tp import shard  # noqa: E402
 
 D, FFN, QKV = 3072, 8192, 5120
@@ -156,6 +156,30 @@ def make_single(device, N, K, M, seed=99):
     return items
 
 
+def make_lmhead(device, fp8, V=128256, D=3072, seed=7):
+    """W [128256 x 3072] ~ N(0, 0.02) as FP16, or FP8-E4M3 with an
+    FP32 per-row scale; x ~ N(0, 1) FP16; FP32 logits plus the greedy argmax."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = torch.randn(V, D, generator=g, device=device) * 0.02
+    x = torch.randn(1, D, generator=g, device=device).half()
+    if fp8:
+        q, rs = quantize_row(w)
+        del w
+        wq, scale = q.view(torch.uint8).contiguous(), rs.contiguous()
+    else:
+        wq, scale = w.half().contiguous(), None
+        del w
+    return [dict(name="lm_head", layer=0, N=V, K=D, split="col", q=wq, s=scale, x=x, fp8=fp8,
+                 y=torch.zeros(1, V, dtype=torch.float32, device=device),
+                 idx=torch.zeros(1, dtype=torch.int32, device=device))]
+
+
+def lm_bytes(it):
+    V, D = it["N"], it["K"]
+    return V * D * (1 if it["fp8"] else 2) + (V * 4 if it["fp8"] else 0) + D * 2 + V * 4
+
+
 # ------------------------------------------------------------------- arms
 
 class OursGemv:
@@ -187,6 +211,41 @@ class RefGemv:
                                      yptr or it["y"].data_ptr(), it["N"], it["K"], stream.cuda_stream)
         if rc != 0:
             raise RuntimeError(f"reference launch failed ({rc})")
+
+
+class OursLmHead:
+    def __init__(self, items, device):
+        self.L = af_lib()
+        it = items[0]
+        self.ws = torch.zeros(self.L.af_lm_head_workspace_bytes(it["N"], it["K"], int(it["fp8"])),
+                              dtype=torch.uint8, device=device)
+
+    def launch(self, stream, it, xptr=None, yptr=None):
+        rc = self.L.af_lm_head_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), int(it["fp8"]),
+                                    it["s"].data_ptr() if it["s"] is not None else None, yptr or it["y"].data_ptr(),
+                                    it["N"], it["K"], it["idx"].data_ptr(), 0, self.ws.data_ptr(), self.ws.numel(),
+                                    stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"af_lm_head_gemv: {self.L.af_status_string(rc).decode()}")
+
+
+class RefLmHead:
+    """The reference's lm_head: its exact cublasGemmEx call (engine.cu:498-512) and its
+    launch_argmax (argmax.cu:92-119), compiled from its sources (oracle/_ref)."""
+
+    def __init__(self, items, device):
+        import oracle
+        self.L = oracle.ref()
+        if self.L is None:
+            raise FileNotFoundError("oracle/_ref/libafref.so (needs the reference sources)")
+
+    def launch(self, stream, it, xptr=None, yptr=None):
+        st = stream.cuda_stream
+        rc = self.L.afref_lm_head(it["q"].data_ptr(), xptr or it["x"].data_ptr(), yptr or it["y"].data_ptr(),
+                                  it["N"], it["K"], st)
+        rc = rc or self.L.afref_argmax(yptr or it["y"].data_ptr(), it["N"], it["idx"].data_ptr(), st)
+        if rc != 0:
+            raise RuntimeError(f"reference lm_head failed ({rc})")
 
 
 def capture_step(arm, items, stream, allreduce=None, pre=None, post=None):
@@ -312,15 +371,25 @@ def main():
         config = {"workload": f"single GEMV {N}x{K} M={M}", "M": M, "copies": len(items),
                   "l2": f"{len(items)} rotating weight copies ({len(items) * N * K / 1e6:.0f} MB) > 4x L2",
                   "parallelism": "single"}
+    elif wl in ("lmhead:f16", "lmhead:fp8"):
+        items = make_lmhead(device, wl.endswith("fp8"))
+        config = {"workload": f"lm_head vocab projection 128256x3072 {wl.split(':')[1].upper()} + greedy argmax "
+                              "(BASELINE config 2)", "M": 1,
+                  "l2": "788 / 394 MB of weights >> 126 MB L2 (no flush needed)", "parallelism": "single"}
     else:
         raise SystemExit(f"unknown workload {wl}")
+    if wl.startswith("lmhead") and world > 1:
+        raise SystemExit("lm_head workloads run on one GPU")
 
-    arm = OursGemv(items, device) if args.impl == "ours" else None
+    lm = wl.startswith("lmhead")
+    arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
     if args.impl == "reference":
         try:
-            arm = RefGemv(items, device)
+            if lm and wl.endswith("fp8"):
+                raise FileNotFoundError("an FP8 lm_head (the reference's lm_head is FP16 cuBLAS only)")
+            arm = RefLmHead(items, device) if lm else RefGemv(items, device)
         except FileNotFoundError as e:
-            print(json.dumps({"impl": "reference", "unavailable": f"{e} not built (needs the reference sources)"}))
+            print(json.dumps({"impl": "reference", "unavailable": f"no reference arm: {e}"}))
             return 0
     stream = torch.cuda.Stream(device)
     allreduce = None
@@ -328,7 +397,8 @@ def main():
         def allreduce(y):
             torch.distributed.all_reduce(y)
 
-    step_bytes = sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items)
+    step_bytes = (sum(lm_bytes(it) for it in items) if lm else
+                  sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items))
     total_bytes = step_bytes * tp
     g = capture_step(arm, items, stream, allreduce)
     sampler = ClockSampler(local) if rank == 0 else None
@@ -345,9 +415,10 @@ def main():
         # copies every output back; graph-captured like the reference's decode.
         xs_host = torch.cat([it["x"].reshape(-1) for it in items]).cpu().pin_memory()
         ys_n = sum(it["y"].numel() for it in items)
-        ys_host = torch.empty(ys_n, dtype=torch.float16).pin_memory()
+        ydt = items[0]["y"].dtype
+        ys_host = torch.empty(ys_n, dtype=ydt).pin_memory()
         xs_dev = torch.empty_like(xs_host, device=device)
-        ys_dev = torch.empty(ys_n, dtype=torch.float16, device=device)
+        ys_dev = torch.empty(ys_n, dtype=ydt, device=device)
         xo, yo = [], []
         ox = oy = 0
         for it in items:
@@ -374,8 +445,8 @@ def main():
         ems, _, _ = time_graph(ge, stream, args.steps, args.warmup, dist_on)
         e2e = {"value": round(total_bytes / (ems / args.steps / 1e3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(ems / args.steps, 5),
-               "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_n * 2),
-               "path": "af_w8a16_gemv C ABI; pinned-host x -> device, 140 GEMVs, outputs -> pinned host; CUDA graph"}
+               "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_n * ys_host.element_size()),
+               "path": ("af_lm_head_gemv" if lm else "af_w8a16_gemv") + " C ABI; pinned-host x -> device, every launch of the step, outputs -> pinned host; CUDA graph"}
     if sampler:
         sampler.stop()
 
@@ -385,7 +456,8 @@ def main():
     peak, peak_kind = measured_peaks()
     per_rank_gbs = step_bytes / (ms_step / 1e3) / 1e9
     out = {
-        "metric": "W8A16 GEMV achieved HBM GB/s (Llama-3.2-3B layer-set stream, M=1)",
+        "metric": ("lm_head vocab projection + argmax achieved HBM GB/s" if lm else
+                   "W8A16 GEMV achieved HBM GB/s (Llama-3.2-3B layer-set stream, M=1)"),
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp8e4m3 weights x fp16 act, fp32 accum",
@@ -395,7 +467,9 @@ def main():
                      "frac": round(per_rank_gbs / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
                      "traffic": traffic_from_profiles(wl, len(items)),
-                     "kernel": "gemv_stream_kernel" if args.impl == "ours" else "w8a16_gemv_kernel (reference)",
+                     "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
+                                 "reference": "cublasGemmEx + argmax (reference)"} if lm else
+                                {"ours": "gemv_fp8_m1_kernel", "reference": "w8a16_gemv_kernel (reference)"})[args.impl],
                      "per_launch": f"{step_bytes / len(items) / 1e6:.2f} MB avg algorithmic bytes / launch over "
                                    f"{ms_step * 1e3 / len(items):.2f} us avg launch (CUDA events over the timed region)"},
         "gpu_launches": launches if args.impl == "ours" else 0,

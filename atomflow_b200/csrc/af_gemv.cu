@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 //     the SM's memory pipe never idles between kernels;
 //   * x arrives by one bulk copy on the TMA engine straight into shared memory,
 //     so it does not queue behind the co-resident CTA's weight requests.
-template <bool GROUP, int kWarps, int kS, int kMinCtas>
+template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
@@ -504,7 +504,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     const int G = gridDim.x, cta = blockIdx.x;
     const int row0 = (int)((long long)cta * p.N / G);
     const int row1 = (int)((long long)(cta + 1) * p.N / G);
-    const int cpt = p.K >> 7;                     // chunks (scale groups) per row
+    constexpr int ESZ = F16 ? 2 : 1;              // weight bytes per element
+    constexpr int CPOS = 128 / ESZ;               // positions per 128-byte chunk
+    const int cpt = (p.K * ESZ) >> 7;             // chunks (FP8: scale groups) per row
     const int T = (row1 - row0 + 15) >> 4;
     const int L = T * cpt;
     const int We = L < kWarps ? L : kWarps;
@@ -538,8 +540,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     const uint8_t* i_p1 = nullptr;
     auto i_rows = [&]() {
         const int r0 = row0 + i_tile * 16 + g;
-        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K + c * 16 : nullptr;
-        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K + c * 16 : nullptr;
+        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K * ESZ + c * 16 : nullptr;
+        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K * ESZ + c * 16 : nullptr;
     };
     i_rows();
     auto issue = [&]() {
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
 
     // ---- compute cursor ----
     const unsigned char* my_ring_p = ring + (size_t)warp * kS * kSlot + lane * 16;
-    const __half* my_x = xs + c * 16;
+    const __half* my_x = xs + c * (16 / ESZ);
     const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
     const float* rs = static_cast<const float*>(p.s);
     int c_tile = wc0 / (cpt > 0 ? cpt : 1);
@@ -653,12 +655,18 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         wh[0] = v1 ? *reinterpret_cast<const uint4*>(sl + 1024) : z;
         wh[1] = v1 ? *reinterpret_cast<const uint4*>(sl + 1536) : z;
         // the lane's 32 positions: [16c, 16c+16) and [64+16c, 64+16c+16) of the chunk
-        const __half* xp_ = my_x + (c_kc << 7);
+        // FP16 weights: the lane's 16 positions [8c, 8c+8) and [32+8c, 32+8c+8)
+        const __half* xp_ = my_x + c_kc * CPOS;
         uint4 xv[4];
-        xv[0] = *reinterpret_cast<const uint4*>(xp_);
-        xv[1] = *reinterpret_cast<const uint4*>(xp_ + 8);
-        xv[2] = *reinterpret_cast<const uint4*>(xp_ + 64);
-        xv[3] = *reinterpret_cast<const uint4*>(xp_ + 72);
+        if (F16) {
+            xv[0] = *reinterpret_cast<const uint4*>(xp_);
+            xv[1] = *reinterpret_cast<const uint4*>(xp_ + 32);
+        } else {
+            xv[0] = *reinterpret_cast<const uint4*>(xp_);
+            xv[1] = *reinterpret_cast<const uint4*>(xp_ + 8);
+            xv[2] = *reinterpret_cast<const uint4*>(xp_ + 64);
+            xv[3] = *reinterpret_cast<const uint4*>(xp_ + 72);
+        }
         float s0 = 1.f, s1 = 1.f;
         if (GROUP) {
             s0 = half_bits_to_float(sp0[c_kc]);
@@ -669,11 +677,22 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         // lane (g, c): bytes 4t..4t+3 of its 32 row bytes are MMA k-step t; its
         // x halves are in the same order, so the permutation of k cancels
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint32_t b0 = u4w(wg[t >> 2], t & 3), b1 = u4w(wh[t >> 2], t & 3);
+        for (int t = 0; t < (F16 ? 4 : 8); ++t) {
+            uint32_t a0, a1, a2, a3;
+            if (F16) {   // halves 4t..4t+3 of the lane's 16
+                a0 = u4w(wg[t >> 1], (t & 1) * 2);
+                a1 = u4w(wh[t >> 1], (t & 1) * 2);
+                a2 = u4w(wg[t >> 1], (t & 1) * 2 + 1);
+                a3 = u4w(wh[t >> 1], (t & 1) * 2 + 1);
+            } else {     // bytes 4t..4t+3 of the lane's 32
+                const uint32_t b0 = u4w(wg[t >> 2], t & 3), b1 = u4w(wh[t >> 2], t & 3);
+                a0 = e4m3x2_lo(b0);
+                a1 = e4m3x2_lo(b1);
+                a2 = e4m3x2_hi(b0);
+                a3 = e4m3x2_hi(b1);
+            }
             float e[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(e, e4m3x2_lo(b0), e4m3x2_lo(b1), e4m3x2_hi(b0), e4m3x2_hi(b1), u4w(xv[t >> 1], (t & 1) * 2),
-                     u4w(xv[t >> 1], (t & 1) * 2 + 1));
+            mma16816(e, a0, a1, a2, a3, u4w(xv[t >> 1], (t & 1) * 2), u4w(xv[t >> 1], (t & 1) * 2 + 1));
 #pragma unroll
             for (int k = 0; k < 4; ++k) d[k] += e[k];
         }
@@ -883,7 +902,6 @@ bool m1_enabled() {
 
 constexpr int kWarpsPerCta = 16;
 constexpr int kRingSlots = 10;   // chunk slots per warp (1 KB each)
-constexpr int kM1Warps = 8;      // warps per CTA of the one-token FP8 kernel (2 CTAs per SM)
 
 template <int WK, int NT>
 cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
@@ -903,10 +921,10 @@ cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cu
     return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
-template <bool GROUP, int NW, int NS>
+template <bool GROUP, bool F16, int NW, int NS>
 cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
     // a ring past ~100 KB means one CTA per SM: registers may grow
-    auto kern = gemv_fp8_m1_kernel<GROUP, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2)>;
+    auto kern = gemv_fp8_m1_kernel<GROUP, F16, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2)>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -995,7 +1013,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     }
     // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
     // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
-    if (wk != W_F16 && M == 1 && K % 128 == 0 && aligned(x, 16) && m1_enabled()) {
+    if (M == 1 && (wk == W_F16 ? K % 64 : K % 128) == 0 && aligned(x, 16) && m1_enabled()) {
         // (warps, ring slots) options, most in-flight bytes first; two CTAs per SM.
         struct Cfg { int nw, ns; };
         const int var = m1_variant();
@@ -1016,8 +1034,10 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
                 prm.sc_bytes = (int)scx;
                 const size_t smem1 = ring1 + xs1 + scx + slots1;
                 cudaError_t e;
-                const bool grp = wk == W_FP8_GROUP;
-#define AF_M1(NW, NS) (grp ? launch_m1<true, NW, NS>(prm, pl, smem1, st) : launch_m1<false, NW, NS>(prm, pl, smem1, st))
+                const bool grp = wk == W_FP8_GROUP, f16 = wk == W_F16;
+#define AF_M1(NW, NS) (grp ? launch_m1<true, false, NW, NS>(prm, pl, smem1, st) \
+                       : f16 ? launch_m1<false, true, NW, NS>(prm, pl, smem1, st) \
+                             : launch_m1<false, false, NW, NS>(prm, pl, smem1, st))
                 if (cf.nw == 8 && cf.ns <= 5) e = cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
                 else if (cf.nw == 16 && cf.ns <= 3) e = cf.ns == 3 ? AF_M1(16, 3) : AF_M1(16, 2);
                 else if (cf.nw == 12) e = cf.ns == 4 ? AF_M1(12, 4) : AF_M1(12, 2);

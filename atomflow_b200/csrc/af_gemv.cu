@@ -495,7 +495,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     unsigned char* ring = smem;
     __half* xs = reinterpret_cast<__half*>(smem + (size_t)kWarps * kS * kSlot);   // x: K halves
     unsigned char* scs = reinterpret_cast<unsigned char*>(xs) + p.xs_bytes;       // staged scales
-    float* wslots = reinterpret_cast<float*>(scs + p.sc_bytes);                  // [kWarps][2][32][4]
+    // warp partials [kWarps][2][32][4] reuse the ring once every warp has finished streaming
+    float* wslots = reinterpret_cast<float*>(ring);
     __shared__ __align__(8) uint64_t s_xbar;
     __shared__ float s_red[kWarps];
     __shared__ int s_redi[kWarps];
@@ -615,6 +616,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     c_rows();
 
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float part0[4] = {0.f, 0.f, 0.f, 0.f}, part1[4] = {0.f, 0.f, 0.f, 0.f};
     const int first_tile = wc0 < wc1 ? c_tile : -1;
     float best_v = 0.f;
     int best_i = -1;
@@ -706,8 +708,11 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             if (seg_lo == c_tile * cpt && j + 1 == (c_tile + 1) * cpt) {
                 emit(c_tile, acc);
             } else {
-                float* dst = wslots + ((size_t)(warp * 2 + (c_tile == first_tile ? 0 : 1)) * 32 + lane) * 4;
-                *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                float* dst = c_tile == first_tile ? part0 : part1;   // registers until the ring is free
+                dst[0] = acc[0];
+                dst[1] = acc[1];
+                dst[2] = acc[2];
+                dst[3] = acc[3];
             }
             acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
             seg_lo = j + 1;
@@ -720,6 +725,11 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     }
     cp_async_wait<0>();
     TRACE(3);
+    __syncthreads();   // every warp is done with the ring
+    *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 0) * 32 + lane) * 4) =
+        make_float4(part0[0], part0[1], part0[2], part0[3]);
+    *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 1) * 32 + lane) * 4) =
+        make_float4(part1[0], part1[1], part1[2], part1[3]);
     __syncthreads();
     TRACE(4);
 
@@ -877,7 +887,7 @@ int m1_variant() {
     static int v = [] {
         const char* e = getenv("AF_M1_VARIANT");
         int k = e ? atoi(e) : 0;
-        return (k >= 0 && k <= 5) ? k : 0;
+        return (k >= 0 && k <= 6) ? k : 0;
     }();
     return v;
 }
@@ -1017,15 +1027,15 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         // (warps, ring slots) options, most in-flight bytes first; two CTAs per SM.
         struct Cfg { int nw, ns; };
         const int var = m1_variant();
-        const Cfg cfgs[6][2] = {{{8, 5}, {8, 3}}, {{16, 3}, {16, 2}}, {{12, 4}, {12, 2}}, {{6, 5}, {6, 3}},
-                                {{8, 12}, {8, 8}}, {{16, 6}, {16, 4}}};
+        const Cfg cfgs[7][3] = {{{8, 5}, {8, 3}, {8, 3}}, {{16, 3}, {16, 2}, {16, 2}}, {{12, 4}, {12, 2}, {12, 2}}, {{6, 5}, {6, 3}, {6, 3}},
+                                {{8, 12}, {8, 8}, {8, 8}}, {{16, 6}, {16, 4}, {16, 4}}, {{8, 5}, {8, 3}, {8, 3}}};
         const size_t xs1 = round_up((size_t)K * 2, 128);
         const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
         for (const Cfg& cf : cfgs[var]) {
             const bool deep = cf.nw * cf.ns * 2 > 100;
             const size_t cap = deep ? kSmemMax - 1024 : (cf.nw <= 6 ? 75 : 113) * 1024;   // 1, 3 or 2 CTAs per SM
-            const size_t slots1 = (size_t)cf.nw * 2 * 32 * 4 * sizeof(float);
-            const size_t ring1 = (size_t)cf.nw * cf.ns * 2048;
+            const size_t slots1 = 0;   // the warp partials reuse the ring
+            const size_t ring1 = (size_t)cf.nw * cf.ns * 2048;   // >= the 1 KB per warp the partials need
             for (size_t scx : {sc1, (size_t)0}) {
                 if (ring1 + slots1 + xs1 + scx > cap) continue;
                 prm.xs_stride = 0;
@@ -1038,7 +1048,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
 #define AF_M1(NW, NS) (grp ? launch_m1<true, false, NW, NS>(prm, pl, smem1, st) \
                        : f16 ? launch_m1<false, true, NW, NS>(prm, pl, smem1, st) \
                              : launch_m1<false, false, NW, NS>(prm, pl, smem1, st))
-                if (cf.nw == 8 && cf.ns <= 5) e = cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
+                if (cf.nw == 8 && cf.ns <= 6) e = cf.ns == 6 ? AF_M1(8, 6) : cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
                 else if (cf.nw == 16 && cf.ns <= 3) e = cf.ns == 3 ? AF_M1(16, 3) : AF_M1(16, 2);
                 else if (cf.nw == 12) e = cf.ns == 4 ? AF_M1(12, 4) : AF_M1(12, 2);
                 else if (cf.nw == 6) e = cf.ns == 5 ? AF_M1(6, 5) : AF_M1(6, 3);

@@ -466,7 +466,7 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(per_rank_gbs / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "traffic": traffic_from_profiles(wl, len(items)),
+                     "traffic": traffic_from_profiles(wl, len(items)) if args.impl == "ours" else None,
                      "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
                                  "reference": "cublasGemmEx + argmax (reference)"} if lm else
                                 {"ours": "gemv_fp8_m1_kernel", "reference": "w8a16_gemv_kernel (reference)"})[args.impl],

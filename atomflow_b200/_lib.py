@@ -59,6 +59,16 @@ C_SYMBOLS = {
     "af_argmax_workspace_bytes": (_sz, [_i]),
     "af_argmax_f32": (_i, [_vp, _i, _vp, _i, _vp, _sz, _vp]),
     "af_argmax_f32_noalloc": (_i, [_vp, _i, _vp, _i, _vp]),
+    "af_tp_create": (_i, [_i, _i, _i, ctypes.POINTER(ctypes.c_void_p)]),
+    "af_tp_ipc_handle": (_i, [_vp, _vp]),
+    "af_tp_open_peers": (_i, [_vp, _vp]),
+    "af_tp_set_peer": (_i, [_vp, _i, _vp]),
+    "af_tp_buffer_bytes": (_sz, [_i]),
+    "af_tp_buffer": (_vp, [_vp]),
+    "af_tp_set_wait_limit_ms": (_i, [_vp, _i]),
+    "af_tp_status": (_i, [_vp, ctypes.POINTER(ctypes.c_int)]),
+    "af_tp_destroy": (_i, [_vp]),
+    "af_w8a16_gemv_allreduce": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "af_view_last_status": (_i, []),
 }
 # C++ launchers with the reference's signatures (include/ops/kernel.h); references are pointers.

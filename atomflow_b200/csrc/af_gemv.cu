@@ -73,6 +73,10 @@ struct GemvParams {
     int* arg_done;        // [1]
     int arg_limit;        // rows >= arg_limit are not argmax candidates
     int pre;              // one-token kernel: ring slots requested before griddepcontrol.wait
+    // tensor-parallel all-reduce epilogue of the one-token kernel (tp_world <= 1: off)
+    int tp_world, tp_rank, tp_nmax;
+    unsigned char* tp_buf[kTpMaxRanks];   // every rank's exchange buffer (TpLayout)
+    unsigned long long tp_wait_ns;
 };
 
 __device__ __forceinline__ uint32_t u4w(const uint4& v, int t) {
@@ -581,6 +585,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.K * 2u);
         bulk_g2s(smem_u32(xs), p.x, (uint32_t)p.K * 2u, smem_u32(&s_xbar));
     }
+    __shared__ unsigned s_ep;   // this launch's epoch (tensor-parallel epilogue)
+    if (p.tp_world > 1 && threadIdx.x == 0)
+        s_ep = ldcg_s32(reinterpret_cast<const int*>(p.tp_buf[p.tp_rank] + TpLayout::epoch) + cta) + 1;
     cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
     mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
@@ -629,7 +636,15 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
             b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
         }
-        if (p.y != nullptr) {
+        if (p.tp_world > 1) {
+            // this rank's partial of rows r0, r1 into every rank's buffer (NVLink stores)
+            const size_t slot = ((size_t)(s_ep & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
+            for (int rr = 0; rr < p.tp_world; ++rr) {
+                float* part = reinterpret_cast<float*>(p.tp_buf[rr] + TpLayout::part) + slot;
+                if (r0 < row1) part[r0] = a;
+                if (r1 < row1) part[r1] = b;
+            }
+        } else if (p.y != nullptr) {
             if (p.y_f32) {
                 if (r0 < row1) static_cast<float*>(p.y)[r0] = a;
                 if (r1 < row1) static_cast<float*>(p.y)[r1] = b;
@@ -750,6 +765,43 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         emit(t, v);
     }
     TRACE(5);
+
+    if (p.tp_world > 1) {
+        // Sum this CTA's rows over the ranks: flag our partials on every rank,
+        // wait (bounded) for the same CTA of every rank, add in rank order.
+        const unsigned ep = s_ep;
+        __threadfence_system();   // each thread's partial stores before the flags (system scope)
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int rr = 0; rr < p.tp_world; ++rr)
+                st_release_sys(reinterpret_cast<unsigned*>(p.tp_buf[rr] + TpLayout::flags) +
+                                   (size_t)p.tp_rank * kTpMaxCtas + cta, ep);
+        }
+        if (threadIdx.x < p.tp_world) {
+            const unsigned* f = reinterpret_cast<const unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::flags) +
+                                (size_t)threadIdx.x * kTpMaxCtas + cta;
+            // a peer is at most one launch ahead (it needs our flags to finish), so >= is exact
+            if ((int)(ld_acquire_sys(f) - ep) < 0) {
+                const uint64_t t0 = globaltimer_ns();
+                while ((int)(ld_acquire_sys(f) - ep) < 0) {
+                    if (globaltimer_ns() - t0 > p.tp_wait_ns) {
+                        atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
+                        break;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        const float* part = reinterpret_cast<const float*>(p.tp_buf[p.tp_rank] + TpLayout::part) +
+                            (size_t)(ep & 1) * kTpMaxRanks * p.tp_nmax;
+        for (int r = row0 + threadIdx.x; r < row1; r += kThreads) {
+            float acc_r = 0.f;
+            for (int rr = 0; rr < p.tp_world; ++rr) acc_r += ldcg_f32(part + (size_t)rr * p.tp_nmax + r);
+            static_cast<__half*>(p.y)[r] = __float2half_rn(acc_r);
+        }
+        if (threadIdx.x == 0)
+            reinterpret_cast<unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::epoch)[cta] = ep;
+    }
 
     if (p.arg_out != nullptr) {
 #pragma unroll
@@ -975,7 +1027,8 @@ bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* 
 
 // Runs one pass of <= 16 tokens.
 af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, void* y, int y_f32, int M, int N,
-                   int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes, cudaStream_t st) {
+                   int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes, cudaStream_t st,
+                   const af_tp_comm* tp = nullptr) {
     int sms = device_sm_count();
     if (sms <= 0) return AF_ERR_CUDA;
     if (!stream_ok(wk, x, w, s, y, K, y_f32) || (arg_out != nullptr && M != 1)) {
@@ -1011,6 +1064,14 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         prm.arg_done = reinterpret_cast<int*>(wsb + pl.off_done);
     }
     prm.arg_limit = arg_limit;
+    if (tp != nullptr) {
+        prm.tp_world = tp->world;
+        prm.tp_rank = tp->rank;
+        prm.tp_nmax = tp->nmax;
+        prm.tp_wait_ns = tp->wait_ns;
+        for (int r = 0; r < tp->world; ++r) prm.tp_buf[r] = tp->peer[r];
+        if (pl.grid > kTpMaxCtas || N > tp->nmax) return AF_ERR_UNSUPPORTED;
+    }
     // Shared memory: the ring, staged x and scales (when they fit), warp partials.
     const size_t ring = (size_t)kWarpsPerCta * kRingSlots * 1024;
     const size_t slots = (size_t)kWarpsPerCta * 2 * 32 * 4 * nt * sizeof(float);
@@ -1059,6 +1120,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
             }
         }
     }
+    if (tp != nullptr) return AF_ERR_UNSUPPORTED;   // the all-reduce epilogue is the one-token kernel's
     const size_t stride = (size_t)K + kXsPad;
     size_t xs = round_up((size_t)M * stride * sizeof(__half), 128);
     if (ring + slots + sc + xs > budget) sc = 0;   // scales from L2 before giving up staged x
@@ -1149,4 +1211,22 @@ extern "C" af_status af_lm_head_gemv(const void* x, const void* w, af_weight_dty
     }
     return run_gemv(wk, static_cast<const __half*>(x), static_cast<const uint8_t*>(w), row_scale,
                     logits, 1, 1, V, D, d_argmax, limit, workspace, workspace_bytes, st);
+}
+
+extern "C" af_status af_w8a16_gemv_allreduce(const void* x, const void* w, const void* scales, void* y, int N,
+                                             int K, int group_size, af_scale_kind kind, af_tp_comm* comm,
+                                             void* stream) {
+    if (comm == nullptr || N <= 0 || K <= 0) return AF_ERR_INVALID;
+    if (kind != AF_SCALE_GROUP_F16 && kind != AF_SCALE_ROW_F32) return AF_ERR_INVALID;
+    if (kind == AF_SCALE_GROUP_F16 && (group_size != 128 || K % 128 != 0)) return AF_ERR_INVALID;
+    if (x == nullptr || w == nullptr || y == nullptr || scales == nullptr || !aligned(y, 2)) return AF_ERR_INVALID;
+    for (int r = 0; r < comm->world; ++r)
+        if (comm->peer[r] == nullptr) return AF_ERR_INVALID;   // peers not opened
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return AF_ERR_INVALID;
+    if (comm->world == 1)
+        return af_w8a16_gemv(x, w, scales, y, 1, N, K, group_size, kind, nullptr, 0, stream);
+    if (K % 128 != 0 || !aligned(x, 16) || !aligned(w, 16) || !m1_enabled()) return AF_ERR_UNSUPPORTED;
+    return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, y, 0, 1,
+                    N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), comm);
 }

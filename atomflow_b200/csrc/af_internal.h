@@ -44,3 +44,31 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
 }
 
 }  // namespace af
+
+// ---- tensor-parallel all-reduce state (af_tp.cu) ----
+namespace af {
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpMaxCtas = 256;
+
+// One rank's exchange buffer; every rank's buffer has the same layout and
+// size, and each rank maps all of them (CUDA IPC or same-process pointers):
+//   [0, 256)            status word (bit 0: a bounded wait gave up)
+//   [256, +1 KB)        per-CTA launch epoch of this rank
+//   [+8 KB)             flags [source rank][CTA]: the epoch that rank's CTA finished
+//   [.., +2*8*nmax*4)   FP32 partials [parity][source rank][nmax]
+struct TpLayout {
+    static constexpr size_t status = 0;
+    static constexpr size_t epoch = 256;
+    static constexpr size_t flags = 256 + kTpMaxCtas * 4;
+    static constexpr size_t part = flags + (size_t)kTpMaxRanks * kTpMaxCtas * 4;
+    static size_t bytes(int nmax) { return part + (size_t)2 * kTpMaxRanks * nmax * 4; }
+};
+}  // namespace af
+
+struct af_tp_comm {
+    int rank, world, nmax, device;
+    unsigned char* buf;                       // this rank's buffer (owned)
+    unsigned char* peer[af::kTpMaxRanks];     // every rank's buffer as mapped here
+    bool ipc_opened[af::kTpMaxRanks];
+    unsigned long long wait_ns;
+};

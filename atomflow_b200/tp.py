@@ -1,12 +1,20 @@
-"""Megatron-style tensor-parallel split of the decode projections.
+"""Tensor parallelism of the decode projections.
 
-Column-parallel projections (fused QKV, gate, up) split the output rows N;
-row-parallel ones (O, down) split K and need a sum (all-reduce) of the
-partial outputs.  K / world stays a multiple of 128 for every shape used here
-(3072/8 = 384, 8192/8 = 1024, 4096/8 = 512, 14336/8 = 1792), so the 128-wide
-scale groups of a K shard are exactly the full matrix's groups: quantising a
-shard gives the same bytes and scales as slicing the quantised matrix.
+* `shard`: Megatron split.  Column-parallel projections (fused QKV, gate, up)
+  split the output rows N; row-parallel ones (O, down) split K and need the
+  partial outputs summed across ranks.  K / world stays a multiple of 128 for
+  every shape used here (3072/8 = 384, 8192/8 = 1024, 4096/8 = 512,
+  14336/8 = 1792), so the 128-wide scale groups of a K shard are exactly the
+  full matrix's groups.
+* `TpComm`: the exchange buffers of af_w8a16_gemv_allreduce (GEMV + all-reduce
+  over NVLink peer memory in one kernel), set up over a torch.distributed
+  group (any backend; only 64-byte IPC handles travel).
 """
+import ctypes
+
+import numpy as np
+
+from ._lib import check, lib
 
 
 def shard(w, x, split, rank, world):
@@ -22,3 +30,30 @@ def shard(w, x, split, rank, world):
     if k % (128 * world):
         raise ValueError(f"K={k} must split into multiples of 128 over {world} ranks")
     return w.chunk(world, 1)[rank], x.chunk(world, x.dim() - 1)[rank]
+
+
+class TpComm:
+    """One rank's exchange buffer, with every peer's buffer mapped (CUDA IPC)."""
+
+    def __init__(self, rank, world, max_n, group=None):
+        import torch.distributed as dist
+        L = lib()
+        self.L = L
+        self.rank, self.world = rank, world
+        self.h = ctypes.c_void_p()
+        check(L.af_tp_create(rank, world, max_n, ctypes.byref(self.h)), "af_tp_create")
+        mine = (ctypes.c_uint8 * 64)()
+        check(L.af_tp_ipc_handle(self.h, mine), "af_tp_ipc_handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(mine), group=group)
+        flat = np.frombuffer(b"".join(handles), dtype=np.uint8).copy()
+        check(L.af_tp_open_peers(self.h, flat.ctypes.data_as(ctypes.c_void_p)), "af_tp_open_peers")
+
+    def gemv_allreduce(self, x, w, s, y, N, K, stream):
+        """y = sum over ranks of this rank's shard W x (FP16), in one kernel."""
+        return self.L.af_w8a16_gemv_allreduce(x, w, s, y, N, K, 128, 0, self.h, stream)
+
+    def status(self):
+        v = ctypes.c_int(0)
+        check(self.L.af_tp_status(self.h, ctypes.byref(v)), "af_tp_status")
+        return v.value

@@ -98,6 +98,38 @@ size_t af_argmax_workspace_bytes(int V);
 af_status af_argmax_f32(const float* logits, int V, int* d_out, af_argmax_mode mode,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------ tensor parallelism (NVLink) ---
+ * Row-parallel projections (O, down) of Megatron tensor parallelism: each of
+ * `world` ranks (one process or one device each) holds a K-shard of W and x
+ * and needs y = sum over ranks of W_r x_r.  af_w8a16_gemv_allreduce computes
+ * its shard and sums across ranks in the same kernel: every CTA stores its
+ * rows' FP32 partials straight into each peer's exchange buffer over NVLink,
+ * raises a flag there, waits (bounded) for the same CTA of every rank, and
+ * sums in rank order (deterministic, identical on every rank).  No counterpart
+ * in the reference (it is single-GPU); this replaces GEMV + NCCL all-reduce.
+ *
+ * Setup is collective: every rank calls af_tp_create, exports its buffer with
+ * af_tp_ipc_handle (64 bytes), exchanges the handles by any transport, and
+ * calls af_tp_open_peers with all `world` handles in rank order.  A process
+ * that drives several GPUs itself can instead call af_tp_set_peer with device
+ * pointers it can reach (peer access enabled).  All ranks must issue the same
+ * sequence of allreduce calls; a wait that runs out (default 2 s,
+ * af_tp_set_wait_limit_ms) sets bit 0 of the status word that af_tp_status
+ * reads, and the kernel finishes with undefined y instead of hanging. */
+typedef struct af_tp_comm af_tp_comm;
+af_status af_tp_create(int rank, int world, int max_n, af_tp_comm** out);
+af_status af_tp_ipc_handle(const af_tp_comm* comm, void* handle64);
+af_status af_tp_open_peers(af_tp_comm* comm, const void* handles /* world x 64 bytes */);
+af_status af_tp_set_peer(af_tp_comm* comm, int peer_rank, void* peer_buffer);
+size_t af_tp_buffer_bytes(int max_n);
+void* af_tp_buffer(const af_tp_comm* comm);
+af_status af_tp_set_wait_limit_ms(af_tp_comm* comm, int ms);
+af_status af_tp_status(const af_tp_comm* comm, int* status);   /* synchronous read */
+af_status af_tp_destroy(af_tp_comm* comm);
+/* One token (M = 1), FP8 weights, K % 128 == 0, x 16-byte aligned, N <= max_n. */
+af_status af_w8a16_gemv_allreduce(const void* x, const void* w, const void* scales, void* y, int N, int K,
+                                  int group_size, af_scale_kind kind, af_tp_comm* comm, void* stream);
+
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for
  * callers that cannot allocate device memory (no cudaMalloc available or

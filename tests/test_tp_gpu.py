@@ -27,7 +27,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, out_q):
     import torch.distributed as dist
     import oracle
     from atomflow_b200.quant import quantize_gs128
@@ -73,7 +73,7 @@ def _rank_main(rank, world, port, q):
     if rank == 0:
         for name in results:
             assert all(gathered[r][name] == gathered[0][name] for r in range(world)), name
-        q.put("ok")
+        out_q.put("ok")
     dist.barrier()
     os._exit(0)
 

@@ -637,12 +637,16 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
         }
         if (p.tp_world > 1) {
-            // this rank's partial of rows r0, r1 into every rank's buffer (NVLink stores)
+            // this rank's partial of rows r0, r1, tagged with the epoch, into
+            // every rank's buffer (NVLink stores to the peers)
             const size_t slot = ((size_t)(s_ep & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
+            const unsigned long long ta = ((unsigned long long)s_ep << 32) | __float_as_uint(a);
+            const unsigned long long tb = ((unsigned long long)s_ep << 32) | __float_as_uint(b);
             for (int rr = 0; rr < p.tp_world; ++rr) {
-                float* part = reinterpret_cast<float*>(p.tp_buf[rr] + TpLayout::part) + slot;
-                if (r0 < row1) part[r0] = a;
-                if (r1 < row1) part[r1] = b;
+                unsigned long long* part =
+                    reinterpret_cast<unsigned long long*>(p.tp_buf[rr] + TpLayout::part) + slot;
+                if (r0 < row1) st_relaxed_sys_u64(part + r0, ta);
+                if (r1 < row1) st_relaxed_sys_u64(part + r1, tb);
             }
         } else if (p.y != nullptr) {
             if (p.y_f32) {
@@ -767,38 +771,33 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     TRACE(5);
 
     if (p.tp_world > 1) {
-        // Sum this CTA's rows over the ranks: flag our partials on every rank,
-        // wait (bounded) for the same CTA of every rank, add in rank order.
+        // Sum this CTA's rows over the ranks, in rank order: each word is
+        // polled (bounded) until it carries this launch's epoch.  A peer is at
+        // most one launch ahead (it cannot finish a launch without our
+        // partials of it), so the other parity half is never overwritten early.
         const unsigned ep = s_ep;
-        __threadfence_system();   // each thread's partial stores before the flags (system scope)
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            for (int rr = 0; rr < p.tp_world; ++rr)
-                st_release_sys(reinterpret_cast<unsigned*>(p.tp_buf[rr] + TpLayout::flags) +
-                                   (size_t)p.tp_rank * kTpMaxCtas + cta, ep);
-        }
-        if (threadIdx.x < p.tp_world) {
-            const unsigned* f = reinterpret_cast<const unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::flags) +
-                                (size_t)threadIdx.x * kTpMaxCtas + cta;
-            // a peer is at most one launch ahead (it needs our flags to finish), so >= is exact
-            if ((int)(ld_acquire_sys(f) - ep) < 0) {
-                const uint64_t t0 = globaltimer_ns();
-                while ((int)(ld_acquire_sys(f) - ep) < 0) {
-                    if (globaltimer_ns() - t0 > p.tp_wait_ns) {
-                        atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
-                        break;
-                    }
-                }
-            }
-        }
-        __syncthreads();
-        const float* part = reinterpret_cast<const float*>(p.tp_buf[p.tp_rank] + TpLayout::part) +
-                            (size_t)(ep & 1) * kTpMaxRanks * p.tp_nmax;
+        const unsigned long long* part =
+            reinterpret_cast<const unsigned long long*>(p.tp_buf[p.tp_rank] + TpLayout::part) +
+            (size_t)(ep & 1) * kTpMaxRanks * p.tp_nmax;
+        bool late = false;
         for (int r = row0 + threadIdx.x; r < row1; r += kThreads) {
             float acc_r = 0.f;
-            for (int rr = 0; rr < p.tp_world; ++rr) acc_r += ldcg_f32(part + (size_t)rr * p.tp_nmax + r);
+            for (int rr = 0; rr < p.tp_world; ++rr) {
+                const unsigned long long* wp = part + (size_t)rr * p.tp_nmax + r;
+                unsigned long long v = ld_relaxed_sys_u64(wp);
+                if ((unsigned)(v >> 32) != ep && !late) {
+                    const uint64_t t0 = globaltimer_ns();
+                    do {
+                        v = ld_relaxed_sys_u64(wp);
+                        if (globaltimer_ns() - t0 > p.tp_wait_ns) { late = true; break; }
+                    } while ((unsigned)(v >> 32) != ep);
+                }
+                acc_r += __uint_as_float((unsigned)v);
+            }
             static_cast<__half*>(p.y)[r] = __float2half_rn(acc_r);
         }
+        if (late) atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
+        __syncthreads();
         if (threadIdx.x == 0)
             reinterpret_cast<unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::epoch)[cta] = ep;
     }

@@ -54,14 +54,15 @@ constexpr int kTpMaxCtas = 256;
 // size, and each rank maps all of them (CUDA IPC or same-process pointers):
 //   [0, 256)            status word (bit 0: a bounded wait gave up)
 //   [256, +1 KB)        per-CTA launch epoch of this rank
-//   [+8 KB)             flags [source rank][CTA]: the epoch that rank's CTA finished
-//   [.., +2*8*nmax*4)   FP32 partials [parity][source rank][nmax]
+//   [.., +2*8*nmax*8)   partials [epoch parity][source rank][nmax], each a 64-bit
+//                       word {launch epoch : 32, FP32 bits : 32}: the data carries
+//                       its own flag, so a reader polls the word itself and no
+//                       fence or separate flag store is needed
 struct TpLayout {
     static constexpr size_t status = 0;
     static constexpr size_t epoch = 256;
-    static constexpr size_t flags = 256 + kTpMaxCtas * 4;
-    static constexpr size_t part = flags + (size_t)kTpMaxRanks * kTpMaxCtas * 4;
-    static size_t bytes(int nmax) { return part + (size_t)2 * kTpMaxRanks * nmax * 4; }
+    static constexpr size_t part = 256 + kTpMaxCtas * 4;
+    static size_t bytes(int nmax) { return part + (size_t)2 * kTpMaxRanks * nmax * 8; }
 };
 }  // namespace af
 

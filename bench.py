@@ -18,8 +18,9 @@ Arms
              reference's path is CUDA, so this arm runs on the GPU.
 
 N > 1 ranks (torchrun): Megatron tensor parallelism of the same layer set --
-QKV/gate/up column-split, O/down row-split followed by an NCCL all-reduce of
-the partial outputs.  Total work is fixed (strong scaling); `value` counts the
+QKV/gate/up column-split, O/down row-split with the partial outputs summed over
+the ranks inside the same kernel through NVLink peer memory
+(af_w8a16_gemv_allreduce; --tp-comm nccl uses a separate NCCL all-reduce).  Total work is fixed (strong scaling); `value` counts the
 bytes all ranks stream divided by the slowest rank's time.
 """
 import argparse
@@ -189,7 +190,15 @@ class OursGemv:
         need = max(self.L.af_w8a16_gemv_workspace_bytes(it["x"].shape[0], it["N"], it["K"], 0) for it in items)
         self.ws = torch.zeros(need, dtype=torch.uint8, device=device)
 
+        self.comm = None
+
     def launch(self, stream, it, xptr=None, yptr=None):
+        if self.comm is not None and it["split"] == "row":
+            rc = self.comm.gemv_allreduce(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
+                                          yptr or it["y"].data_ptr(), it["N"], it["K"], stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"af_w8a16_gemv_allreduce: {self.L.af_status_string(rc).decode()}")
+            return
         rc = self.L.af_w8a16_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
                                   yptr or it["y"].data_ptr(), it["x"].shape[0], it["N"], it["K"], 128, 0,
                                   self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream)
@@ -338,6 +347,8 @@ def main():
     ap.add_argument("--workload", default="layerset")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",
+                    help="N > 1: all-reduce of row-split outputs inside the GEMV kernel (fused) or by NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -393,9 +404,16 @@ def main():
             return 0
     stream = torch.cuda.Stream(device)
     allreduce = None
-    if tp > 1:
+    comm = None
+    if tp > 1 and args.tp_comm == "nccl":
         def allreduce(y):
             torch.distributed.all_reduce(y)
+    elif tp > 1:
+        # row-split projections: one kernel computes the partial GEMV and sums it
+        # over the ranks through NVLink peer memory (af_w8a16_gemv_allreduce)
+        from atomflow_b200.tp import TpComm
+        comm = TpComm(trank, tp, max(it["N"] for it in items))
+        arm.comm = comm
 
     step_bytes = (sum(lm_bytes(it) for it in items) if lm else
                   sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items))
@@ -449,6 +467,11 @@ def main():
                "path": ("af_lm_head_gemv" if lm else "af_w8a16_gemv") + " C ABI; pinned-host x -> device, every launch of the step, outputs -> pinned host; CUDA graph"}
     if sampler:
         sampler.stop()
+    if comm is not None and comm.status() != 0:
+        raise RuntimeError("af_w8a16_gemv_allreduce: a peer wait ran out (status word set)")
+    if tp > 1:
+        config["tp_allreduce"] = ("fused into the GEMV over NVLink peer memory" if comm is not None
+                                  else "NCCL all_reduce after the GEMV")
 
     if rank != 0:
         finish(dist_on)

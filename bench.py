@@ -91,8 +91,12 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.samples.append((time.time(), [c.strip() for c in line.split(",")]))
 
-    def mark(self):
-        return time.time()
+    def wait_first(self, limit_s=5.0):
+        """Block until nvidia-smi has printed a sample (it needs ~1 s to start),
+        so that a short timed region still has samples within 250 ms of it."""
+        t_end = time.time() + limit_s
+        while self.ok and not self.samples and time.time() < t_end:
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is not None:
@@ -418,8 +422,10 @@ def main():
     step_bytes = (sum(lm_bytes(it) for it in items) if lm else
                   sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items))
     total_bytes = step_bytes * tp
-    g = capture_step(arm, items, stream, allreduce)
     sampler = ClockSampler(local) if rank == 0 else None
+    g = capture_step(arm, items, stream, allreduce)
+    if sampler:
+        sampler.wait_first()
     ms, t0, t1 = time_graph(g, stream, args.steps, args.warmup, dist_on)
     clocks = sampler.summary(t0, t1) if sampler else None
     ms_step = ms / args.steps

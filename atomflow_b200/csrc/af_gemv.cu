@@ -577,6 +577,10 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     // our own x fetch do not wait behind a full prefetch.
 #pragma unroll 1
     for (int q = 0; q < p.pre; ++q) issue();
+    // x may be written by the kernel this one waits for, so it is read only
+    // after the wait; an L2 prefetch now is only a hint (L2 is the point of
+    // coherence) and turns that read into an L2 hit when x was not just written.
+    if (threadIdx.x == 32) bulk_prefetch_l2(p.x, (uint32_t)p.K * 2u);
 
     pdl_wait();
     TRACE(1);

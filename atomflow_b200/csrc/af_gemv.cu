@@ -756,14 +756,14 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     __syncthreads();
     TRACE(4);
 
+    // 32-bit index arithmetic: L = tiles x chunks per row stays far below 2^31 / kWarps
     for (int t = warp; t < T; t += kWarps) {
-        const int wa_ = (int)owner_of((long long)t * cpt, L, We);
-        const int wb_ = (int)owner_of((long long)(t + 1) * cpt - 1, L, We);
+        const int wa_ = ((t * cpt + 1) * We - 1) / L;
+        const int wb_ = ((t + 1) * cpt * We - 1) / L;
         if (wa_ == wb_) continue;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
         for (int w = wa_; w <= wb_; ++w) {
-            const int w0 = (int)((long long)w * L / We);
-            const int slot = (t == w0 / cpt) ? 0 : 1;
+            const int slot = (t * cpt <= (w * L) / We) ? 0 : 1;   // w's first tile is t?
             const float4 f = *reinterpret_cast<const float4*>(wslots + ((size_t)(w * 2 + slot) * 32 + lane) * 4);
             v[0] += f.x;
             v[1] += f.y;

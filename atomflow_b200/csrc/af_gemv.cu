@@ -85,9 +85,11 @@ __device__ __forceinline__ uint32_t u4w(const uint4& v, int t) {
 
 #ifdef AF_EXP_TRACE
 __device__ unsigned long long g_trace[64][160][6];
+__device__ long long g_trace_clk[64][160][6];
 __device__ unsigned int g_trace_launch;
-#define TRACE(k) do { if (threadIdx.x == 0 && blockIdx.x < 160) { g_trace[s_tl % 64][blockIdx.x][k] = globaltimer_ns(); } } while (0)
+#define TRACE(k) do { if (threadIdx.x == 0 && blockIdx.x < 160) { g_trace_clk[s_tl % 64][blockIdx.x][k] = clock64(); g_trace[s_tl % 64][blockIdx.x][k] = globaltimer_ns(); } } while (0)
 extern "C" void af_exp_trace_read(unsigned long long* dst) { cudaMemcpyFromSymbol(dst, g_trace, sizeof(g_trace)); }
+extern "C" void af_exp_trace_clk(long long* dst) { cudaMemcpyFromSymbol(dst, g_trace_clk, sizeof(g_trace_clk)); }
 #else
 #define TRACE(k) do {} while (0)
 #endif
@@ -504,6 +506,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     __shared__ __align__(8) uint64_t s_xbar;
     __shared__ float s_red[kWarps];
     __shared__ int s_redi[kWarps];
+    __shared__ int s_wstart[kWarps + 1];   // first chunk of each warp; [kWarps] = L
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, c = lane & 3;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -521,7 +524,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&s_xbar), 1);
         mbar_init_fence();
+        s_wstart[kWarps] = L;
     }
+    if (lane == 0) s_wstart[warp] = wc0;
     __syncthreads();
 
     // staged scales: bytes [sc_lo, ...) of the [N, G] FP16 array
@@ -756,20 +761,24 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     __syncthreads();
     TRACE(4);
 
-    // 32-bit index arithmetic: L = tiles x chunks per row stays far below 2^31 / kWarps
+    // Tiles split between warps: sum the owners' partials in warp order.  The
+    // owners come from the warp-start table (no divisions on this serial tail).
     for (int t = warp; t < T; t += kWarps) {
-        const int wa_ = ((t * cpt + 1) * We - 1) / L;
-        const int wb_ = ((t + 1) * cpt * We - 1) / L;
-        if (wa_ == wb_) continue;
+        const int lo = t * cpt, hi = lo + cpt;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w = wa_; w <= wb_; ++w) {
-            const int slot = (t * cpt <= (w * L) / We) ? 0 : 1;   // w's first tile is t?
+        int owners = 0;
+        for (int w = 0; w < kWarps; ++w) {
+            const int a = s_wstart[w], b = s_wstart[w + 1];
+            if (a >= b || a >= hi || b <= lo) continue;
+            ++owners;
+            const int slot = a >= lo ? 0 : 1;   // t is w's first tile -> part0
             const float4 f = *reinterpret_cast<const float4*>(wslots + ((size_t)(w * 2 + slot) * 32 + lane) * 4);
             v[0] += f.x;
             v[1] += f.y;
             v[2] += f.z;
             v[3] += f.w;
         }
+        if (owners < 2) continue;   // one owner: emitted from the main loop
         emit(t, v);
     }
     TRACE(5);

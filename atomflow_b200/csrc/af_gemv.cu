@@ -40,6 +40,7 @@
 //     the epilogue (per-CTA candidates in the caller's workspace, the last CTA
 //     reduces them and returns the workspace to zero).
 
+#include <algorithm>
 #include <cuda_fp8.h>
 #include <cstdio>
 #include <cstdlib>
@@ -75,6 +76,8 @@ struct GemvParams {
     int pre;              // one-token kernel: ring slots requested before griddepcontrol.wait
     // tensor-parallel all-reduce epilogue of the one-token kernel (tp_world <= 1: off)
     int tp_world, tp_rank, tp_nmax;
+    int tp_arg;           // 1: the exchange is the argmax pair (vocab-parallel lm_head), not the rows
+    int arg_off;          // global index of this rank's row 0 (vocab-parallel lm_head)
     unsigned char* tp_buf[kTpMaxRanks];   // every rank's exchange buffer (TpLayout)
     unsigned long long tp_wait_ns;
 };
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
             b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
         }
-        if (p.tp_world > 1) {
+        if (p.tp_world > 1 && !p.tp_arg) {
             // this rank's partial of rows r0, r1, tagged with the epoch, into
             // every rank's buffer (NVLink stores to the peers)
             const size_t slot = ((size_t)(s_ep & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
@@ -783,7 +786,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     }
     TRACE(5);
 
-    if (p.tp_world > 1) {
+    if (p.tp_world > 1 && !p.tp_arg) {
         // Sum this CTA's rows over the ranks, in rank order: each word is
         // polled (bounded) until it carries this launch's epoch.  A peer is at
         // most one launch ahead (it cannot finish a launch without our
@@ -860,6 +863,49 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                     if (argmax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                }
+                if (p.tp_world > 1 && p.tp_arg) {
+                    // vocab-parallel: push (max, global index) to every rank, then
+                    // reduce all ranks' pairs (lane r polls rank r, bounded)
+                    const unsigned ep = (unsigned)ldcg_s32(reinterpret_cast<const int*>(
+                                            p.tp_buf[p.tp_rank] + TpLayout::lm_epoch)) + 1u;
+                    const size_t pslot = ((size_t)(ep & 1) * kTpMaxRanks + p.tp_rank) * 2;
+                    const int gi = bi >= 0 ? bi + p.arg_off : -1;
+                    if (lane < p.tp_world) {
+                        unsigned long long* dst =
+                            reinterpret_cast<unsigned long long*>(p.tp_buf[lane] + TpLayout::lm_pair) + pslot;
+                        st_relaxed_sys_u64(dst, ((unsigned long long)ep << 32) | __float_as_uint(bv));
+                        st_relaxed_sys_u64(dst + 1, ((unsigned long long)ep << 32) | (unsigned)gi);
+                    }
+                    float rv = 0.f;
+                    int ri = -1;
+                    if (lane < p.tp_world) {
+                        const unsigned long long* src =
+                            reinterpret_cast<const unsigned long long*>(p.tp_buf[p.tp_rank] + TpLayout::lm_pair) +
+                            ((size_t)(ep & 1) * kTpMaxRanks + lane) * 2;
+                        unsigned long long a = ld_relaxed_sys_u64(src), b = ld_relaxed_sys_u64(src + 1);
+                        if ((unsigned)(a >> 32) != ep || (unsigned)(b >> 32) != ep) {
+                            const uint64_t t0 = globaltimer_ns();
+                            bool late = false;
+                            do {
+                                a = ld_relaxed_sys_u64(src);
+                                b = ld_relaxed_sys_u64(src + 1);
+                                if (globaltimer_ns() - t0 > p.tp_wait_ns) { late = true; break; }
+                            } while ((unsigned)(a >> 32) != ep || (unsigned)(b >> 32) != ep);
+                            if (late) atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
+                        }
+                        const bool fresh = (unsigned)(a >> 32) == ep && (unsigned)(b >> 32) == ep;
+                        rv = fresh ? __uint_as_float((unsigned)a) : 0.f;   // a late rank is no candidate
+                        ri = fresh ? (int)(unsigned)b : -1;
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, rv, o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, ri, o);
+                        if (argmax_better(ov, oi, rv, ri)) { rv = ov; ri = oi; }
+                    }
+                    bi = ri;
+                    if (lane == 0) reinterpret_cast<unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::lm_epoch)[0] = ep;
                 }
                 if (lane == 0) {
                     *p.arg_out = bi;
@@ -1040,7 +1086,7 @@ bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* 
 // Runs one pass of <= 16 tokens.
 af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, void* y, int y_f32, int M, int N,
                    int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes, cudaStream_t st,
-                   const af_tp_comm* tp = nullptr) {
+                   const af_tp_comm* tp = nullptr, int tp_arg_off = 0) {
     int sms = device_sm_count();
     if (sms <= 0) return AF_ERR_CUDA;
     if (!stream_ok(wk, x, w, s, y, K, y_f32) || (arg_out != nullptr && M != 1)) {
@@ -1081,8 +1127,10 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         prm.tp_rank = tp->rank;
         prm.tp_nmax = tp->nmax;
         prm.tp_wait_ns = tp->wait_ns;
+        prm.tp_arg = arg_out != nullptr;
+        prm.arg_off = tp_arg_off;
         for (int r = 0; r < tp->world; ++r) prm.tp_buf[r] = tp->peer[r];
-        if (pl.grid > kTpMaxCtas || N > tp->nmax) return AF_ERR_UNSUPPORTED;
+        if (arg_out == nullptr && (pl.grid > kTpMaxCtas || N > tp->nmax)) return AF_ERR_UNSUPPORTED;
     }
     // Shared memory: the ring, staged x and scales (when they fit), warp partials.
     const size_t ring = (size_t)kWarpsPerCta * kRingSlots * 1024;
@@ -1241,4 +1289,32 @@ extern "C" af_status af_w8a16_gemv_allreduce(const void* x, const void* w, const
     if (K % 128 != 0 || !aligned(x, 16) || !aligned(w, 16) || !m1_enabled()) return AF_ERR_UNSUPPORTED;
     return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, y, 0, 1,
                     N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), comm);
+}
+
+extern "C" af_status af_lm_head_gemv_tp(const void* x, const void* w, af_weight_dtype w_dtype, const float* row_scale,
+                                        float* logits, int V_local, int D, int vocab_offset, int* d_argmax,
+                                        af_argmax_mode mode, void* workspace, size_t workspace_bytes,
+                                        af_tp_comm* comm, void* stream) {
+    if (comm == nullptr || V_local <= 0 || D <= 0 || vocab_offset < 0 || d_argmax == nullptr) return AF_ERR_INVALID;
+    if (w_dtype != AF_W_F16 && w_dtype != AF_W_FP8_E4M3) return AF_ERR_INVALID;
+    if ((w_dtype == AF_W_F16) != (row_scale == nullptr)) return AF_ERR_INVALID;
+    if (mode != AF_ARGMAX_TRUE && mode != AF_ARGMAX_REF_COMPAT) return AF_ERR_INVALID;
+    if (x == nullptr || w == nullptr || !aligned(d_argmax, 4) || (logits != nullptr && !aligned(logits, 4)))
+        return AF_ERR_INVALID;
+    for (int r = 0; r < comm->world; ++r)
+        if (comm->peer[r] == nullptr) return AF_ERR_INVALID;   // peers not opened
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return AF_ERR_INVALID;
+    if (comm->world == 1)
+        return af_lm_head_gemv(x, w, w_dtype, row_scale, logits, V_local, D, d_argmax, mode, workspace,
+                               workspace_bytes, stream);
+    const int wk = (w_dtype == AF_W_F16) ? W_F16 : W_FP8_ROW;
+    if ((wk == W_F16 ? D % 64 : D % 128) != 0 || !aligned(x, 16) || !aligned(w, 16) || !m1_enabled())
+        return AF_ERR_UNSUPPORTED;
+    // ref-compat: only global ids < 65536 are candidates
+    long long lim = V_local;
+    if (mode == AF_ARGMAX_REF_COMPAT) lim = std::max(0ll, std::min<long long>(V_local, 65536ll - vocab_offset));
+    return run_gemv(wk, static_cast<const __half*>(x), static_cast<const uint8_t*>(w), row_scale, logits, 1, 1,
+                    V_local, D, d_argmax, (int)lim, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                    comm, vocab_offset);
 }

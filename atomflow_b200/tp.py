@@ -53,6 +53,13 @@ class TpComm:
         """y = sum over ranks of this rank's shard W x (FP16), in one kernel."""
         return self.L.af_w8a16_gemv_allreduce(x, w, s, y, N, K, 128, 0, self.h, stream)
 
+    def lm_head_argmax(self, x, w, fp8, row_scale, logits, V_local, D, vocab_offset, d_argmax, mode, ws, ws_bytes,
+                       stream):
+        """Vocab-parallel lm_head: this rank's rows [vocab_offset, +V_local); the
+        global greedy token lands in d_argmax on every rank."""
+        return self.L.af_lm_head_gemv_tp(x, w, 1 if fp8 else 0, row_scale, logits, V_local, D, vocab_offset,
+                                         d_argmax, mode, ws, ws_bytes, self.h, stream)
+
     def status(self):
         v = ctypes.c_int(0)
         check(self.L.af_tp_status(self.h, ctypes.byref(v)), "af_tp_status")

@@ -103,10 +103,11 @@ af_status af_argmax_f32(const float* logits, int V, int* d_out, af_argmax_mode m
  * `world` ranks (one process or one device each) holds a K-shard of W and x
  * and needs y = sum over ranks of W_r x_r.  af_w8a16_gemv_allreduce computes
  * its shard and sums across ranks in the same kernel: every CTA stores its
- * rows' FP32 partials straight into each peer's exchange buffer over NVLink,
- * raises a flag there, waits (bounded) for the same CTA of every rank, and
- * sums in rank order (deterministic, identical on every rank).  No counterpart
- * in the reference (it is single-GPU); this replaces GEMV + NCCL all-reduce.
+ * rows' FP32 partials, tagged with the launch epoch, straight into each
+ * peer's exchange buffer over NVLink, polls (bounded) until every rank's
+ * words for its rows carry that epoch, and sums in rank order (deterministic,
+ * identical on every rank).  No counterpart in the reference (it is
+ * single-GPU); this replaces GEMV + NCCL all-reduce.
  *
  * Setup is collective: every rank calls af_tp_create, exports its buffer with
  * af_tp_ipc_handle (64 bytes), exchanges the handles by any transport, and
@@ -129,6 +130,19 @@ af_status af_tp_destroy(af_tp_comm* comm);
 /* One token (M = 1), FP8 weights, K % 128 == 0, x 16-byte aligned, N <= max_n. */
 af_status af_w8a16_gemv_allreduce(const void* x, const void* w, const void* scales, void* y, int N, int K,
                                   int group_size, af_scale_kind kind, af_tp_comm* comm, void* stream);
+/* Vocab-parallel lm_head + greedy argmax: rank r holds rows [vocab_offset,
+ * vocab_offset + V_local) of the lm_head weight (any split; offsets
+ * increasing with rank).  Each rank projects its rows (local logits to
+ * `logits` when not NULL) and takes its local argmax; the last CTA pushes the
+ * (max, global index) pair to every rank and reduces all ranks' pairs, so
+ * *d_argmax (device int, required) holds the same global token on every
+ * rank, ties to the lowest index.  AF_ARGMAX_REF_COMPAT limits candidates to
+ * global ids < 65536.  Same weight formats as af_lm_head_gemv; one-token
+ * kernel only (16-byte aligned x and W, D % 128 == 0 for FP8, D % 64 for FP16). */
+af_status af_lm_head_gemv_tp(const void* x, const void* w, af_weight_dtype w_dtype, const float* row_scale,
+                             float* logits, int V_local, int D, int vocab_offset, int* d_argmax,
+                             af_argmax_mode mode, void* workspace, size_t workspace_bytes, af_tp_comm* comm,
+                             void* stream);
 
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for

@@ -4,6 +4,9 @@
   over gloo; each rank holds a K-shard of a row-parallel projection; the fused
   GEMV + NVLink all-reduce must equal the unsharded FP64 oracle on every rank,
   bit-identically across ranks, over repeated calls and a graph replay.
+* Vocab-parallel lm_head (two GPUs): each rank projects its slice of the
+  vocabulary; the exchanged argmax must equal the argmax of all ranks' local
+  logits (gathered), on every rank, in true and reference-compatible modes.
 * One GPU: a peer that never arrives (its flags are never set) makes the
   bounded wait run out; the kernel must finish, set the status word, and
   leave the GPU usable.  No second waiting kernel runs anywhere.
@@ -78,19 +81,90 @@ def _rank_main(rank, world, port, out_q):
     os._exit(0)
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_gemv_allreduce_two_gpus():
+def _lm_rank_main(rank, world, port, out_q):
+    import torch.distributed as dist
+    import oracle
+    from atomflow_b200 import lib
+    from atomflow_b200.tp import TpComm
+    from tests._util import assert_fp32_close
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    L = lib()
+    comm = TpComm(rank, world, 64)
+    st = torch.cuda.Stream()
+    checked = []
+    # (V, D, fp8, split point): uneven splits; the FP8 case straddles id 65536
+    for V, D, fp8, cut in [(20000, 3072, False, 12345), (70016, 1024, True, 40000)]:
+        g = torch.Generator().manual_seed(V)
+        w = torch.randn(V, D, generator=g) * 0.02
+        x = torch.randn(1, D, generator=g).half()
+        if fp8:
+            rs = (w.abs().amax(1) / 448).clamp_min(1e-12)
+            q = (w / rs[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+            wfull, sfull = q, rs.float()
+        else:
+            wfull, sfull = w.half(), None
+        lo, hi = (0, cut) if rank == 0 else (cut, V)
+        wd = wfull[lo:hi].contiguous().cuda()
+        sd = sfull[lo:hi].contiguous().cuda() if fp8 else None
+        xd = x.cuda()
+        logits = torch.zeros(hi - lo, dtype=torch.float32, device="cuda")
+        ws = torch.zeros(L.af_lm_head_workspace_bytes(hi - lo, D, 1 if fp8 else 0), dtype=torch.uint8, device="cuda")
+        for mode in (0, 1):
+            idx = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+            with torch.cuda.stream(st):
+                for _ in range(3):   # repeated calls: the exchange epoch advances
+                    rc = comm.lm_head_argmax(xd.data_ptr(), wd.data_ptr(), fp8, sd.data_ptr() if fp8 else None,
+                                             logits.data_ptr(), hi - lo, D, lo, idx.data_ptr(), mode, ws.data_ptr(),
+                                             ws.numel(), st.cuda_stream)
+                    assert rc == 0, rc
+            st.synchronize()
+            parts = [None] * world
+            dist.all_gather_object(parts, logits.cpu().numpy())
+            full = np.concatenate(parts)
+            want = oracle.argmax(full, mode)
+            assert int(idx.item()) == want, (V, mode, int(idx.item()), want)
+            checked.append(int(idx.item()))
+        # local logits against the FP64 oracle
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        if fp8:
+            ref = oracle.gemv_f64(xb, wfull[lo:hi].numpy(), sfull[lo:hi].numpy(), "row")
+        else:
+            ref = oracle.gemv_f64(xb, wfull[lo:hi].view(torch.int16).numpy().view(np.uint16), None, "f16")
+        assert_fp32_close(logits.cpu().numpy(), ref.ravel(), f"lm_head V={V} rank {rank}")
+    assert comm.status() == 0
+    gathered = [None] * world
+    dist.all_gather_object(gathered, checked)
+    if rank == 0:
+        assert gathered[0] == gathered[1]
+        out_q.put("ok")
+    dist.barrier()
+    os._exit(0)
+
+
+def _spawn(target, world=2):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
     assert q.get(timeout=5) == "ok"
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_lm_head_vocab_parallel_two_gpus():
+    _spawn(_lm_rank_main)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gemv_allreduce_two_gpus():
+    _spawn(_rank_main)
 
 
 def test_gemv_allreduce_missing_peer_times_out_with_status():
@@ -131,4 +205,28 @@ def test_gemv_allreduce_argument_errors():
     assert L.af_tp_create(0, 2, 4096, ctypes.byref(h)) == 0
     # peers not opened yet
     assert L.af_w8a16_gemv_allreduce(16, 16, 16, 16, 64, 128, 128, 0, h, None) == 1
+    assert L.af_tp_destroy(h) == 0
+
+
+def test_lm_head_tp_missing_peer_times_out_with_status():
+    from atomflow_b200 import lib
+    L = lib()
+    h = ctypes.c_void_p()
+    assert L.af_tp_create(0, 2, 64, ctypes.byref(h)) == 0
+    ghost = torch.zeros(L.af_tp_buffer_bytes(64), dtype=torch.uint8, device="cuda")
+    assert L.af_tp_set_peer(h, 1, ghost.data_ptr()) == 0
+    assert L.af_tp_set_wait_limit_ms(h, 50) == 0
+    V, D = 4096, 1024
+    w = (torch.randn(V, D, device="cuda") * 0.02).half()
+    x = torch.randn(1, D, device="cuda").half()
+    ws = torch.zeros(L.af_lm_head_workspace_bytes(V, D, 0), dtype=torch.uint8, device="cuda")
+    idx = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.af_lm_head_gemv_tp(x.data_ptr(), w.data_ptr(), 0, None, None, V, D, 0, idx.data_ptr(), 0,
+                                ws.data_ptr(), ws.numel(), h, st) == 0
+    torch.cuda.synchronize()
+    status = ctypes.c_int(0)
+    assert L.af_tp_status(h, ctypes.byref(status)) == 0
+    assert status.value & 1
+    assert 0 <= int(idx.item()) < V   # the local candidate survives a missing peer
     assert L.af_tp_destroy(h) == 0

@@ -161,9 +161,10 @@ def make_single(device, N, K, M, seed=99):
     return items
 
 
-def make_lmhead(device, fp8, V=128256, D=3072, seed=7):
+def make_lmhead(device, fp8, rank=0, world=1, V=128256, D=3072, seed=7):
     """W [128256 x 3072] ~ N(0, 0.02) as FP16, or FP8-E4M3 with an
-    FP32 per-row scale; x ~ N(0, 1) FP16; FP32 logits plus the greedy argmax."""
+    FP32 per-row scale; x ~ N(0, 1) FP16; FP32 logits plus the greedy argmax.
+    world > 1: this rank's vocab rows [rank*V/world, (rank+1)*V/world)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     w = torch.randn(V, D, generator=g, device=device) * 0.02
@@ -175,8 +176,12 @@ def make_lmhead(device, fp8, V=128256, D=3072, seed=7):
     else:
         wq, scale = w.half().contiguous(), None
         del w
-    return [dict(name="lm_head", layer=0, N=V, K=D, split="col", q=wq, s=scale, x=x, fp8=fp8,
-                 y=torch.zeros(1, V, dtype=torch.float32, device=device),
+    lo, hi = rank * V // world, (rank + 1) * V // world
+    if world > 1:
+        wq = wq[lo:hi].contiguous()
+        scale = scale[lo:hi].contiguous() if scale is not None else None
+    return [dict(name="lm_head", layer=0, N=hi - lo, K=D, off=lo, split="col", q=wq, s=scale, x=x, fp8=fp8,
+                 y=torch.zeros(1, hi - lo, dtype=torch.float32, device=device),
                  idx=torch.zeros(1, dtype=torch.int32, device=device))]
 
 
@@ -232,8 +237,18 @@ class OursLmHead:
         it = items[0]
         self.ws = torch.zeros(self.L.af_lm_head_workspace_bytes(it["N"], it["K"], int(it["fp8"])),
                               dtype=torch.uint8, device=device)
+        self.comm = None
 
     def launch(self, stream, it, xptr=None, yptr=None):
+        if self.comm is not None:   # vocab-parallel: the argmax pairs cross NVLink in the same kernel
+            rc = self.comm.lm_head_argmax(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["fp8"],
+                                          it["s"].data_ptr() if it["s"] is not None else None,
+                                          yptr or it["y"].data_ptr(), it["N"], it["K"], it["off"],
+                                          it["idx"].data_ptr(), 0, self.ws.data_ptr(), self.ws.numel(),
+                                          stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"af_lm_head_gemv_tp: {self.L.af_status_string(rc).decode()}")
+            return
         rc = self.L.af_lm_head_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), int(it["fp8"]),
                                     it["s"].data_ptr() if it["s"] is not None else None, yptr or it["y"].data_ptr(),
                                     it["N"], it["K"], it["idx"].data_ptr(), 0, self.ws.data_ptr(), self.ws.numel(),
@@ -387,14 +402,13 @@ def main():
                   "l2": f"{len(items)} rotating weight copies ({len(items) * N * K / 1e6:.0f} MB) > 4x L2",
                   "parallelism": "single"}
     elif wl in ("lmhead:f16", "lmhead:fp8"):
-        items = make_lmhead(device, wl.endswith("fp8"))
+        items = make_lmhead(device, wl.endswith("fp8"), trank, tp)
         config = {"workload": f"lm_head vocab projection 128256x3072 {wl.split(':')[1].upper()} + greedy argmax "
                               "(BASELINE config 2)", "M": 1,
-                  "l2": "788 / 394 MB of weights >> 126 MB L2 (no flush needed)", "parallelism": "single"}
+                  "l2": "788 / 394 MB of weights >> 126 MB L2 (no flush needed)",
+                  "parallelism": f"vocab-parallel tp{tp}" if tp > 1 else "single"}
     else:
         raise SystemExit(f"unknown workload {wl}")
-    if wl.startswith("lmhead") and world > 1:
-        raise SystemExit("lm_head workloads run on one GPU")
 
     lm = wl.startswith("lmhead")
     arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
@@ -409,6 +423,8 @@ def main():
     stream = torch.cuda.Stream(device)
     allreduce = None
     comm = None
+    if tp > 1 and wl.startswith("lmhead") and args.tp_comm == "nccl":
+        raise SystemExit("vocab-parallel lm_head exchanges its argmax inside the kernel (--tp-comm fused)")
     if tp > 1 and args.tp_comm == "nccl":
         def allreduce(y):
             torch.distributed.all_reduce(y)
@@ -416,7 +432,7 @@ def main():
         # row-split projections: one kernel computes the partial GEMV and sums it
         # over the ranks through NVLink peer memory (af_w8a16_gemv_allreduce)
         from atomflow_b200.tp import TpComm
-        comm = TpComm(trank, tp, max(it["N"] for it in items))
+        comm = TpComm(trank, tp, max(it["N"] for it in items) if not wl.startswith("lmhead") else 64)
         arm.comm = comm
 
     step_bytes = (sum(lm_bytes(it) for it in items) if lm else
@@ -476,7 +492,8 @@ def main():
     if comm is not None and comm.status() != 0:
         raise RuntimeError("af_w8a16_gemv_allreduce: a peer wait ran out (status word set)")
     if tp > 1:
-        config["tp_allreduce"] = ("fused into the GEMV over NVLink peer memory" if comm is not None
+        config["tp_allreduce"] = (("argmax (max, index) pairs exchanged inside the lm_head kernel over NVLink"
+                                   if lm else "fused into the GEMV over NVLink peer memory") if comm is not None
                                   else "NCCL all_reduce after the GEMV")
 
     if rank != 0:

@@ -70,6 +70,10 @@ C_SYMBOLS = {
     "af_tp_destroy": (_i, [_vp]),
     "af_w8a16_gemv_allreduce": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "af_lm_head_gemv_tp": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp, _i, _vp, _sz, _vp, _vp]),
+    "af_rmsnorm_w8a16_gemv": (_i, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "af_w8a16_gemv_residual": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "af_rmsnorm_w8a16_swiglu": (_i, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "af_w8a16_gemv_allreduce_residual": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "af_view_last_status": (_i, []),
 }
 # C++ launchers with the reference's signatures (include/ops/kernel.h); references are pointers.

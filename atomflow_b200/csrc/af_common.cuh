@@ -149,6 +149,20 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // System-scope release store / acquire load of a flag in (possibly peer) memory.
+// The arithmetic of the reference's element-wise kernels, which are built with
+// --use_fast_math (flush-to-zero, approximate division and square root):
+// the PTX instructions themselves, so that fused epilogues round identically.
+__device__ __forceinline__ float fdiv_full_ftz(float a, float b) {
+    float r;
+    asm("div.full.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float rsqrt_approx_ftz(float a) {
+    float r;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
+}
+
 // 64-bit single-copy-atomic accesses visible across GPUs (peer memory over NVLink)
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

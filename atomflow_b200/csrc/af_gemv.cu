@@ -76,6 +76,15 @@ struct GemvParams {
     int pre;              // one-token kernel: ring slots requested before griddepcontrol.wait
     // tensor-parallel all-reduce epilogue of the one-token kernel (tp_world <= 1: off)
     int tp_world, tp_rank, tp_nmax;
+    // fused prologue / epilogues of the one-token kernel (all null: a plain GEMV)
+    const float* norm_w;  // RMSNorm weight FP32 [K]: x is normalised in shared memory first
+    float norm_eps;
+    int gam_bytes;        // shared bytes reserved for the staged norm weight
+    __half* xn_out;       // optional: the normalised x (CTA 0 writes it)
+    const __half* res;    // residual FP16 [N]: y = half(res + half(Wx)) (may alias y)
+    __half* aux;          // optional: residual mode -> half(Wx) [N]; gate/up mode -> [gate | up] FP16 [2N]
+    const uint8_t* w2;    // gate/up mode: the up weights (p.w: gate), y = half(silu(gate) * up)
+    const void* s2;       // gate/up mode: the up scales
     int tp_arg;           // 1: the exchange is the argmax pair (vocab-parallel lm_head), not the rows
     int arg_off;          // global index of this rank's row 0 (vocab-parallel lm_head)
     unsigned char* tp_buf[kTpMaxRanks];   // every rank's exchange buffer (TpLayout)
@@ -489,7 +498,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 //     the SM's memory pipe never idles between kernels;
 //   * x arrives by one bulk copy on the TMA engine straight into shared memory,
 //     so it does not queue behind the co-resident CTA's weight requests.
-template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas>
+//   * PAIR (gate/up + SwiGLU): a 16-row MMA tile holds 8 gate rows and the same
+//     8 up rows, so each lane owns gate[r] and up[r] and applies the
+//     activation in registers.
+template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas, bool PAIR>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
@@ -518,7 +530,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     constexpr int ESZ = F16 ? 2 : 1;              // weight bytes per element
     constexpr int CPOS = 128 / ESZ;               // positions per 128-byte chunk
     const int cpt = (p.K * ESZ) >> 7;             // chunks (FP8: scale groups) per row
-    const int T = (row1 - row0 + 15) >> 4;
+    constexpr int TR = PAIR ? 8 : 16;             // output rows per MMA tile
+    const int T = (row1 - row0 + TR - 1) / TR;
     const int L = T * cpt;
     const int We = L < kWarps ? L : kWarps;
     const int wc0 = warp < We ? (int)((long long)warp * L / We) : L;
@@ -534,11 +547,22 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
 
     // staged scales: bytes [sc_lo, ...) of the [N, G] FP16 array
     const size_t sc_lo = p.sc_bytes ? ((size_t)row0 * cpt * 2) & ~(size_t)15 : 0;
+    const int sc_half = PAIR ? p.sc_bytes / 2 : 0;   // gate/up mode: up scales at scs + sc_half
     if (GROUP && p.sc_bytes) {
         const size_t sc_hi = ((size_t)row1 * cpt * 2 + 15) & ~(size_t)15;
-        const unsigned char* sb = static_cast<const unsigned char*>(p.s);
-        for (size_t o = sc_lo + (size_t)threadIdx.x * 16; o < sc_hi; o += (size_t)kThreads * 16)
-            cp_async16(smem_u32(scs + (o - sc_lo)), sb + o);
+#pragma unroll
+        for (int m = 0; m < (PAIR ? 2 : 1); ++m) {
+            const unsigned char* sb = static_cast<const unsigned char*>(m ? p.s2 : p.s);
+            for (size_t o = sc_lo + (size_t)threadIdx.x * 16; o < sc_hi; o += (size_t)kThreads * 16)
+                cp_async16(smem_u32(scs + m * sc_half + (o - sc_lo)), sb + o);
+        }
+    }
+    // RMSNorm weight (a constant: staged before the wait)
+    float* gam = reinterpret_cast<float*>(scs + p.sc_bytes);
+    if (p.norm_w != nullptr) {
+        const unsigned char* gb = reinterpret_cast<const unsigned char*>(p.norm_w);
+        for (int o = threadIdx.x * 16; o < p.K * 4; o += kThreads * 16)
+            cp_async16(smem_u32(reinterpret_cast<unsigned char*>(gam) + o), gb + o);
     }
     cp_async_commit();
 
@@ -552,9 +576,14 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     const uint8_t* i_p0 = nullptr;
     const uint8_t* i_p1 = nullptr;
     auto i_rows = [&]() {
-        const int r0 = row0 + i_tile * 16 + g;
-        i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K * ESZ + c * 16 : nullptr;
-        i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K * ESZ + c * 16 : nullptr;
+        const int r0 = row0 + i_tile * TR + g;
+        if (PAIR) {
+            i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K + c * 16 : nullptr;
+            i_p1 = r0 < row1 ? p.w2 + (size_t)r0 * p.K + c * 16 : nullptr;
+        } else {
+            i_p0 = r0 < row1 ? p.w + (size_t)r0 * p.K * ESZ + c * 16 : nullptr;
+            i_p1 = r0 + 8 < row1 ? p.w + (size_t)(r0 + 8) * p.K * ESZ + c * 16 : nullptr;
+        }
     };
     i_rows();
     auto issue = [&]() {
@@ -603,6 +632,34 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
     mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
+    if (p.norm_w != nullptr) {
+        // RMSNorm of x in place, in the reference's arithmetic order
+        // (src/kernel/rmsnorm.cu:9-67, 128 threads): per-thread strided FMA
+        // sums, each warp's shuffle-down tree, the warps' sums in order, then
+        // rsqrt(sum / K + eps) and half(x * r * w).
+        __shared__ float s_nrm[4];
+        __shared__ float s_rms;
+        if (threadIdx.x < 128) {
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < p.K; i += 128) {
+                const float v = __half2float(xs[i]);
+                ss = fmaf(v, v, ss);
+            }
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) ss += __shfl_down_sync(0xffffffffu, ss, o);
+            if (lane == 0) s_nrm[warp] = ss;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            s_rms = rsqrt_approx_ftz(fdiv_full_ftz(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], (float)p.K) +
+                                     p.norm_eps);
+        __syncthreads();
+        const float r = s_rms;
+        for (int i = threadIdx.x; i < p.K; i += kThreads) xs[i] = __float2half_rn(__half2float(xs[i]) * r * gam[i]);
+        __syncthreads();
+        if (p.xn_out != nullptr && cta == 0)
+            for (int i = threadIdx.x; i < p.K; i += kThreads) p.xn_out[i] = xs[i];
+    }
 #pragma unroll 1
     for (int q = p.pre; q < kS; ++q) issue();
     TRACE(2);
@@ -618,10 +675,19 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     const uint16_t* sp0 = nullptr;   // scales of rows g, g+8 (shared or global)
     const uint16_t* sp1 = nullptr;
     auto c_rows = [&]() {
-        const int r0 = row0 + c_tile * 16 + g;
+        const int r0 = row0 + c_tile * TR + g;
         v0 = r0 < row1;
-        v1 = r0 + 8 < row1;
-        if (GROUP) {
+        v1 = PAIR ? v0 : r0 + 8 < row1;
+        if (PAIR) {
+            const int a0 = v0 ? r0 : row0;
+            if (p.sc_bytes) {
+                sp0 = reinterpret_cast<const uint16_t*>(scs + (size_t)a0 * cpt * 2 - sc_lo);
+                sp1 = reinterpret_cast<const uint16_t*>(scs + sc_half + (size_t)a0 * cpt * 2 - sc_lo);
+            } else {
+                sp0 = s16 + (size_t)a0 * cpt;
+                sp1 = static_cast<const uint16_t*>(p.s2) + (size_t)a0 * cpt;
+            }
+        } else if (GROUP) {
             const int a0 = v0 ? r0 : row0, a1 = v1 ? r0 + 8 : row0;
             if (p.sc_bytes) {
                 sp0 = reinterpret_cast<const uint16_t*>(scs + (size_t)a0 * cpt * 2 - sc_lo);
@@ -642,8 +708,23 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
 
     auto emit = [&](int tile, const float (&v)[4]) {
         if (c != 0) return;   // token 0 sits in MMA column 0 (lanes c == 0)
-        const int r0 = row0 + tile * 16 + g, r1 = r0 + 8;
+        const int r0 = row0 + tile * TR + g, r1 = r0 + 8;
         float a = v[0], b = v[2];
+        if (PAIR) {
+            // gate and up rounded to FP16 as the reference stores them, then its
+            // SwiGLU (src/kernel/swiglu.cu:12-26): half(g / (1 + e^-g) * u)
+            if (r0 < row1) {
+                const __half gh = __float2half_rn(a), uh = __float2half_rn(b);
+                const float gf = __half2float(gh);
+                const float silu = fdiv_full_ftz(gf, 1.0f + __expf(-gf));
+                static_cast<__half*>(p.y)[r0] = __float2half_rn(silu * __half2float(uh));
+                if (p.aux != nullptr) {
+                    p.aux[r0] = gh;
+                    p.aux[p.N + r0] = uh;
+                }
+            }
+            return;
+        }
         if (!GROUP && rs != nullptr) {
             a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
             b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
@@ -665,8 +746,19 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                 if (r0 < row1) static_cast<float*>(p.y)[r0] = a;
                 if (r1 < row1) static_cast<float*>(p.y)[r1] = b;
             } else {
-                if (r0 < row1) static_cast<__half*>(p.y)[r0] = __float2half_rn(a);
-                if (r1 < row1) static_cast<__half*>(p.y)[r1] = __float2half_rn(b);
+                // residual: half(res + half(Wx)) as the reference's residual add
+                // (src/kernel/residual_add.cu:11-20) applied to the stored output
+                __half ya = __float2half_rn(a), yb = __float2half_rn(b);
+                if (p.aux != nullptr) {
+                    if (r0 < row1) p.aux[r0] = ya;
+                    if (r1 < row1) p.aux[r1] = yb;
+                }
+                if (p.res != nullptr) {
+                    if (r0 < row1) ya = __float2half_rn(__half2float(p.res[r0]) + __half2float(ya));
+                    if (r1 < row1) yb = __float2half_rn(__half2float(p.res[r1]) + __half2float(yb));
+                }
+                if (r0 < row1) static_cast<__half*>(p.y)[r0] = ya;
+                if (r1 < row1) static_cast<__half*>(p.y)[r1] = yb;
             }
         }
         if (p.arg_out != nullptr) {
@@ -810,7 +902,10 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                 }
                 acc_r += __uint_as_float((unsigned)v);
             }
-            static_cast<__half*>(p.y)[r] = __float2half_rn(acc_r);
+            __half yh = __float2half_rn(acc_r);
+            if (p.aux != nullptr) p.aux[r] = yh;
+            if (p.res != nullptr) yh = __float2half_rn(__half2float(p.res[r]) + __half2float(yh));
+            static_cast<__half*>(p.y)[r] = yh;
         }
         if (late) atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
         __syncthreads();
@@ -1041,10 +1136,10 @@ cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cu
     return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
-template <bool GROUP, bool F16, int NW, int NS>
+template <bool GROUP, bool F16, int NW, int NS, bool PAIR = false>
 cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
     // a ring past ~100 KB means one CTA per SM: registers may grow
-    auto kern = gemv_fp8_m1_kernel<GROUP, F16, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2)>;
+    auto kern = gemv_fp8_m1_kernel<GROUP, F16, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2), PAIR>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -1084,13 +1179,25 @@ bool stream_ok(int wk, const void* x, const void* w, const void* s, const void* 
 }
 
 // Runs one pass of <= 16 tokens.
+// Fused prologue / epilogues of the one-token kernel (GemvParams has the meaning).
+struct Fused {
+    const float* norm_w = nullptr;
+    float eps = 0.f;
+    __half* xn_out = nullptr;
+    const __half* res = nullptr;
+    __half* aux = nullptr;
+    const uint8_t* w2 = nullptr;   // non-null: gate/up + SwiGLU
+    const void* s2 = nullptr;
+};
+
 af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, void* y, int y_f32, int M, int N,
                    int K, int* arg_out, int arg_limit, void* ws, size_t ws_bytes, cudaStream_t st,
-                   const af_tp_comm* tp = nullptr, int tp_arg_off = 0) {
+                   const af_tp_comm* tp = nullptr, int tp_arg_off = 0, const Fused* fz = nullptr) {
+    const bool pair = fz != nullptr && fz->w2 != nullptr;
     int sms = device_sm_count();
     if (sms <= 0) return AF_ERR_CUDA;
     if (!stream_ok(wk, x, w, s, y, K, y_f32) || (arg_out != nullptr && M != 1)) {
-        if (arg_out != nullptr) return AF_ERR_UNSUPPORTED;
+        if (arg_out != nullptr || tp != nullptr || fz != nullptr) return AF_ERR_UNSUPPORTED;
         const int skind = (wk == W_FP8_GROUP) ? AF_SCALE_GROUP_F16 : (wk == W_FP8_ROW) ? AF_SCALE_ROW_F32 : AF_SCALE_NONE;
         dim3 grid((N + 7) / 8, M);
         cudaError_t e = launch_pdl(gemv_simple_kernel, grid, dim3(256), 0, st, w, (int)(wk == W_F16), s, skind,
@@ -1122,6 +1229,15 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         prm.arg_done = reinterpret_cast<int*>(wsb + pl.off_done);
     }
     prm.arg_limit = arg_limit;
+    if (fz != nullptr) {
+        prm.norm_w = fz->norm_w;
+        prm.norm_eps = fz->eps;
+        prm.xn_out = fz->xn_out;
+        prm.res = fz->res;
+        prm.aux = fz->aux;
+        prm.w2 = fz->w2;
+        prm.s2 = fz->s2;
+    }
     if (tp != nullptr) {
         prm.tp_world = tp->world;
         prm.tp_rank = tp->rank;
@@ -1137,11 +1253,13 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     const size_t slots = (size_t)kWarpsPerCta * 2 * 32 * 4 * nt * sizeof(float);
     const size_t budget = kSmemMax - 1024;   // static shared and alignment
     size_t sc = 0;
-    if (wk == W_FP8_GROUP && aligned(s, 16) && ((size_t)N * (K / 128) * 2) % 16 == 0) {
+    if (wk == W_FP8_GROUP && aligned(s, 16) && ((size_t)N * (K / 128) * 2) % 16 == 0 &&
+        (!pair || aligned(fz->s2, 16))) {
         const size_t rows = (size_t)(N + pl.grid - 1) / pl.grid;
-        sc = round_up(rows * (K / 128) * 2 + 32, 128);
+        sc = round_up(rows * (K / 128) * 2 + 32, 128) * (pair ? 2 : 1);
         if (ring + slots + sc > budget || sc > 32 * 1024) sc = 0;
     }
+    const size_t gam = (fz != nullptr && fz->norm_w != nullptr) ? round_up((size_t)K * 4, 128) : 0;
     // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
     // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
     if (M == 1 && (wk == W_F16 ? K % 64 : K % 128) == 0 && aligned(x, 16) && m1_enabled()) {
@@ -1151,22 +1269,24 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         const Cfg cfgs[7][3] = {{{8, 5}, {8, 3}, {8, 3}}, {{16, 3}, {16, 2}, {16, 2}}, {{12, 4}, {12, 2}, {12, 2}}, {{6, 5}, {6, 3}, {6, 3}},
                                 {{8, 12}, {8, 8}, {8, 8}}, {{16, 6}, {16, 4}, {16, 4}}, {{8, 5}, {8, 3}, {8, 3}}};
         const size_t xs1 = round_up((size_t)K * 2, 128);
-        const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
+        const size_t sc1 = (sc && sc <= (pair ? 32 : 16) * 1024) ? sc : 0;
         for (const Cfg& cf : cfgs[var]) {
             const bool deep = cf.nw * cf.ns * 2 > 100;
             const size_t cap = deep ? kSmemMax - 1024 : (cf.nw <= 6 ? 75 : 113) * 1024;   // 1, 3 or 2 CTAs per SM
             const size_t slots1 = 0;   // the warp partials reuse the ring
             const size_t ring1 = (size_t)cf.nw * cf.ns * 2048;   // >= the 1 KB per warp the partials need
             for (size_t scx : {sc1, (size_t)0}) {
-                if (ring1 + slots1 + xs1 + scx > cap) continue;
+                if (ring1 + slots1 + xs1 + scx + gam > cap) continue;
                 prm.xs_stride = 0;
                 prm.pre = m1_pre(cf.ns);
                 prm.xs_bytes = (int)xs1;
                 prm.sc_bytes = (int)scx;
-                const size_t smem1 = ring1 + xs1 + scx + slots1;
+                prm.gam_bytes = (int)gam;
+                const size_t smem1 = ring1 + xs1 + scx + gam + slots1;
                 cudaError_t e;
                 const bool grp = wk == W_FP8_GROUP, f16 = wk == W_F16;
-#define AF_M1(NW, NS) (grp ? launch_m1<true, false, NW, NS>(prm, pl, smem1, st) \
+#define AF_M1(NW, NS) (pair ? launch_m1<true, false, NW, NS, true>(prm, pl, smem1, st) \
+                       : grp ? launch_m1<true, false, NW, NS>(prm, pl, smem1, st) \
                        : f16 ? launch_m1<false, true, NW, NS>(prm, pl, smem1, st) \
                              : launch_m1<false, false, NW, NS>(prm, pl, smem1, st))
                 if (cf.nw == 8 && cf.ns <= 6) e = cf.ns == 6 ? AF_M1(8, 6) : cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
@@ -1180,7 +1300,8 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
             }
         }
     }
-    if (tp != nullptr) return AF_ERR_UNSUPPORTED;   // the all-reduce epilogue is the one-token kernel's
+    // the all-reduce and the fused prologue / epilogues are the one-token kernel's
+    if (tp != nullptr || fz != nullptr) return AF_ERR_UNSUPPORTED;
     const size_t stride = (size_t)K + kXsPad;
     size_t xs = round_up((size_t)M * stride * sizeof(__half), 128);
     if (ring + slots + sc + xs > budget) sc = 0;   // scales from L2 before giving up staged x
@@ -1317,4 +1438,84 @@ extern "C" af_status af_lm_head_gemv_tp(const void* x, const void* w, af_weight_
     return run_gemv(wk, static_cast<const __half*>(x), static_cast<const uint8_t*>(w), row_scale, logits, 1, 1,
                     V_local, D, d_argmax, (int)lim, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                     comm, vocab_offset);
+}
+
+// ------------------------------------------------- fused decode-layer ops
+namespace {
+af_status fused_checks(const void* x, const void* w, const void* scales, const void* y, int N, int K,
+                       int group_size, af_scale_kind kind) {
+    if (N <= 0 || K <= 0 || x == nullptr || w == nullptr || y == nullptr || scales == nullptr) return AF_ERR_INVALID;
+    if (kind != AF_SCALE_GROUP_F16 && kind != AF_SCALE_ROW_F32) return AF_ERR_INVALID;
+    if (kind == AF_SCALE_GROUP_F16 && group_size != 128) return AF_ERR_INVALID;
+    if (K % 128 != 0 || !aligned(y, 2)) return AF_ERR_INVALID;
+    if (!aligned(x, 16) || !aligned(w, 16) || !m1_enabled()) return AF_ERR_UNSUPPORTED;
+    return AF_OK;
+}
+}  // namespace
+
+extern "C" af_status af_rmsnorm_w8a16_gemv(const void* x, const float* norm_w, float eps, const void* w,
+                                          const void* scales, void* y, int N, int K, int group_size,
+                                          af_scale_kind kind, void* x_norm_out, void* stream) {
+    af_status r = fused_checks(x, w, scales, y, N, K, group_size, kind);
+    if (r != AF_OK) return r;
+    if (norm_w == nullptr || !aligned(norm_w, 16) || (x_norm_out != nullptr && !aligned(x_norm_out, 2)))
+        return AF_ERR_INVALID;
+    Fused fz;
+    fz.norm_w = norm_w;
+    fz.eps = eps;
+    fz.xn_out = static_cast<__half*>(x_norm_out);
+    return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, y, 0, 1,
+                    N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, 0, &fz);
+}
+
+extern "C" af_status af_w8a16_gemv_residual(const void* x, const void* w, const void* scales, void* inout, int N,
+                                           int K, int group_size, af_scale_kind kind, void* y_out, void* stream) {
+    af_status r = fused_checks(x, w, scales, inout, N, K, group_size, kind);
+    if (r != AF_OK) return r;
+    if (y_out != nullptr && !aligned(y_out, 2)) return AF_ERR_INVALID;
+    Fused fz;
+    fz.res = static_cast<const __half*>(inout);
+    fz.aux = static_cast<__half*>(y_out);
+    return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, inout, 0,
+                    1, N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, 0, &fz);
+}
+
+extern "C" af_status af_rmsnorm_w8a16_swiglu(const void* x, const float* norm_w, float eps, const void* w_gate,
+                                            const void* s_gate, const void* w_up, const void* s_up, void* h, int N,
+                                            int K, int group_size, af_scale_kind kind, void* gate_up_out,
+                                            void* x_norm_out, void* stream) {
+    af_status r = fused_checks(x, w_gate, s_gate, h, N, K, group_size, kind);
+    if (r != AF_OK) return r;
+    if (w_up == nullptr || s_up == nullptr) return AF_ERR_INVALID;
+    if (kind != AF_SCALE_GROUP_F16 || !aligned(w_up, 16)) return AF_ERR_UNSUPPORTED;
+    if (norm_w != nullptr && !aligned(norm_w, 16)) return AF_ERR_INVALID;
+    if ((gate_up_out != nullptr && !aligned(gate_up_out, 2)) || (x_norm_out != nullptr && !aligned(x_norm_out, 2)))
+        return AF_ERR_INVALID;
+    if (norm_w == nullptr && x_norm_out != nullptr) return AF_ERR_INVALID;
+    Fused fz;
+    fz.norm_w = norm_w;
+    fz.eps = eps;
+    fz.xn_out = static_cast<__half*>(x_norm_out);
+    fz.aux = static_cast<__half*>(gate_up_out);
+    fz.w2 = static_cast<const uint8_t*>(w_up);
+    fz.s2 = s_up;
+    return run_gemv(W_FP8_GROUP, static_cast<const __half*>(x), static_cast<const uint8_t*>(w_gate), s_gate, h, 0,
+                    1, N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), nullptr, 0, &fz);
+}
+
+extern "C" af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const void* scales, void* inout,
+                                                     int N, int K, int group_size, af_scale_kind kind,
+                                                     af_tp_comm* comm, void* stream) {
+    if (comm == nullptr) return AF_ERR_INVALID;
+    af_status r = fused_checks(x, w, scales, inout, N, K, group_size, kind);
+    if (r != AF_OK) return r;
+    for (int q = 0; q < comm->world; ++q)
+        if (comm->peer[q] == nullptr) return AF_ERR_INVALID;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return AF_ERR_INVALID;
+    Fused fz;
+    fz.res = static_cast<const __half*>(inout);
+    return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, inout, 0,
+                    1, N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream),
+                    comm->world > 1 ? comm : nullptr, 0, &fz);
 }

@@ -144,6 +144,36 @@ af_status af_lm_head_gemv_tp(const void* x, const void* w, af_weight_dtype w_dty
                              af_argmax_mode mode, void* workspace, size_t workspace_bytes, af_tp_comm* comm,
                              void* stream);
 
+/* ------------------------------------------------ fused decode-layer ops ---
+ * The reference runs RMSNorm, GEMV, SwiGLU and residual add as separate
+ * kernels (src/core/engine.cu:292-483; src/kernel/rmsnorm.cu, swiglu.cu,
+ * residual_add.cu).  These fold the element-wise work into the one-token
+ * GEMV, with the reference's rounding points kept (the normalised x, gate and
+ * up, and the GEMV output are rounded to FP16 where the reference stores them):
+ *   af_rmsnorm_w8a16_gemv    y = W . half(rmsnorm(x) * norm_w)     (QKV)
+ *   af_w8a16_gemv_residual   inout = half(inout + half(W . x))     (O, down)
+ *   af_rmsnorm_w8a16_swiglu  h = half(silu(half(Wg . xn)) * half(Wu . xn)),
+ *                            xn = rmsnorm(x) (norm_w NULL: xn = x) (gate/up)
+ * RMSNorm: r = 1 / sqrt(sum(x^2) / K + eps), xn = half(x * r * norm_w), norm_w
+ * FP32 [K] 16-byte aligned.  Optional outputs for checking each stage:
+ * x_norm_out FP16 [K], y_out FP16 [N] (before the residual), gate_up_out FP16
+ * [2N] (gate then up).  One token, FP8 weights, K % 128 == 0, x and W 16-byte
+ * aligned (else AF_ERR_UNSUPPORTED); SwiGLU needs FP16 group scales. */
+af_status af_rmsnorm_w8a16_gemv(const void* x, const float* norm_w, float eps, const void* w, const void* scales,
+                                void* y, int N, int K, int group_size, af_scale_kind kind, void* x_norm_out,
+                                void* stream);
+af_status af_w8a16_gemv_residual(const void* x, const void* w, const void* scales, void* inout, int N, int K,
+                                 int group_size, af_scale_kind kind, void* y_out, void* stream);
+af_status af_rmsnorm_w8a16_swiglu(const void* x, const float* norm_w, float eps, const void* w_gate,
+                                  const void* s_gate, const void* w_up, const void* s_up, void* h, int N, int K,
+                                  int group_size, af_scale_kind kind, void* gate_up_out, void* x_norm_out,
+                                  void* stream);
+/* Row-parallel projection + all-reduce + residual in one kernel:
+ * inout = half(inout + half(sum over ranks of W_r x_r)). */
+af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const void* scales, void* inout, int N,
+                                           int K, int group_size, af_scale_kind kind, af_tp_comm* comm,
+                                           void* stream);
+
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for
  * callers that cannot allocate device memory (no cudaMalloc available or

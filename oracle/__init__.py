@@ -72,6 +72,12 @@ def ref():
         L.afref_argmax.argtypes = [vp, i, vp, vp]
         L.afref_lm_head.restype = i
         L.afref_lm_head.argtypes = [vp, vp, vp, i, i, vp]
+        L.afref_rms_norm.restype = i
+        L.afref_rms_norm.argtypes = [vp, vp, vp, i, ctypes.c_float, vp]
+        L.afref_swiglu.restype = i
+        L.afref_swiglu.argtypes = [vp, vp, vp, i, vp]
+        L.afref_residual_add.restype = i
+        L.afref_residual_add.argtypes = [vp, vp, i, vp]
         _ref = L
     return _ref
 

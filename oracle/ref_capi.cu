@@ -2,7 +2,7 @@
 // and for bench.py's reference arm.  TEST INFRASTRUCTURE ONLY.
 //
 // Linked, by oracle/Makefile, with the unmodified AtomFlow sources
-// src/kernel/qkv_gemm.cu and src/kernel/argmax.cu, compiled in place with the
+// src/kernel/{qkv_gemm,argmax,rmsnorm,swiglu,residual_add}.cu, compiled in place with the
 // reference's release flags (-O3 --use_fast_math -DNDEBUG, CMakeLists.txt
 // :12-14,117-131) for sm_100a.  Nothing here re-implements the reference; each
 // function builds the reference's Views and calls its launcher.
@@ -43,4 +43,30 @@ extern "C" int afref_lm_head(const void* w, const void* x, float* logits, int V,
                                      CUDA_R_16F, D, x, CUDA_R_16F, D, &beta, logits, CUDA_R_32F, V,
                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
     return st == CUBLAS_STATUS_SUCCESS ? (int)cudaGetLastError() : -(int)st;
+}
+
+// The engine's RMSNorm call (src/core/engine.cu:294,409): FP16 [1,D] in, FP32 weight, eps 1e-5.
+extern "C" int afref_rms_norm(const void* x, const float* w, void* out, int D, float eps, void* stream) {
+    View xv = create_contiguous_view(const_cast<void*>(x), DataType::FP16, {1, D});
+    View wv = create_contiguous_view(const_cast<float*>(w), DataType::FP32, {D});
+    View ov = create_contiguous_view(out, DataType::FP16, {1, D});
+    launch_rms_norm(xv, wv, ov, eps, static_cast<cudaStream_t>(stream));
+    return (int)cudaGetLastError();
+}
+
+// src/core/engine.cu:448: out = silu(gate) * up (FP16), in place over gate there.
+extern "C" int afref_swiglu(const void* gate, const void* up, void* out, int N, void* stream) {
+    View gv = create_contiguous_view(const_cast<void*>(gate), DataType::FP16, {1, N});
+    View uv = create_contiguous_view(const_cast<void*>(up), DataType::FP16, {1, N});
+    View ov = create_contiguous_view(out, DataType::FP16, {1, N});
+    launch_swiglu(gv, uv, ov, static_cast<cudaStream_t>(stream));
+    return (int)cudaGetLastError();
+}
+
+// src/core/engine.cu:401,483: inout += sub (FP16, in place).
+extern "C" int afref_residual_add(void* inout, const void* sub, int N, void* stream) {
+    View iv = create_contiguous_view(inout, DataType::FP16, {1, N});
+    View sv = create_contiguous_view(const_cast<void*>(sub), DataType::FP16, {1, N});
+    launch_residual_add(iv, sv, static_cast<cudaStream_t>(stream));
+    return (int)cudaGetLastError();
 }

@@ -1,0 +1,188 @@
+"""GPU parity of the fused decode-layer ops (RMSNorm prologue, residual and
+SwiGLU epilogues) through the C ABI.
+
+Each fused stage is checked where the reference rounds:
+  * x_norm: bit-identical to the reference's own rms_norm kernel
+    (src/kernel/rmsnorm.cu, compiled from its sources into oracle/_ref);
+  * the projection of x_norm: bit-identical to the unfused af_w8a16_gemv of
+    the same x_norm, and within the GEMV tolerance of the FP64 oracle and of
+    the reference kernel's bit-exact restatement;
+  * residual: bit-identical to half(res + y) with y the pre-residual output;
+  * SwiGLU: gate and up each within the GEMV tolerance; h bit-identical to the
+    reference's swiglu kernel applied to them.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from tests._util import assert_fp16_parity, fp16_bits, make_gemv_case, normal_f32
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+EPS = 1e-5
+
+
+def lib():
+    from atomflow_b200 import lib as _l
+    return _l()
+
+
+def ref():
+    r = oracle.ref()
+    if r is None:
+        pytest.skip("oracle/_ref/libafref.so not built")
+    return r
+
+
+def dev(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    return torch.from_numpy(a).cuda()
+
+
+def host16(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy().view(np.uint16).reshape(-1)
+
+
+def st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def gemv(xd, qd, sd, N, K):
+    y = torch.zeros(N, dtype=torch.int16, device="cuda")
+    assert lib().af_w8a16_gemv(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), y.data_ptr(), 1, N, K, 128, 0,
+                               None, 0, st()) == 0
+    return y
+
+
+def ref_rmsnorm(xd, gd, K):
+    out = torch.zeros(K, dtype=torch.int16, device="cuda")
+    assert ref().afref_rms_norm(xd.data_ptr(), gd.data_ptr(), out.data_ptr(), K, EPS, st()) == 0
+    return out
+
+
+def norm_inputs(seed, K, x_std):
+    x = fp16_bits(normal_f32(seed, (1, K), x_std))
+    gam = (1.0 + normal_f32(seed + 7, (K,), 0.1)).astype(np.float32)
+    return x, gam
+
+
+def check_gemv(y_bits, x_bits, q, s, what):
+    ref64 = oracle.gemv_f64(x_bits, q, s, "group", with_l2=True)
+    rk = oracle.gemv_refmath(x_bits, q, s, nthreads=8)
+    assert_fp16_parity(y_bits, ref64, what, ref_kernel_bits=rk)
+
+
+@pytest.mark.parametrize("N,K,x_std", [(5120, 3072, 1.0), (1000, 1024, 0.04), (3072, 3072, 30.0)])
+def test_rmsnorm_gemv(N, K, x_std):
+    L = lib()
+    x, gam = norm_inputs(N + K, K, x_std)
+    _, q, s = make_gemv_case(N, 1, N, K)
+    xd, gd, qd, sd = dev(x), dev(gam), dev(q), dev(s)
+    y = torch.zeros(N, dtype=torch.int16, device="cuda")
+    xn = torch.zeros(K, dtype=torch.int16, device="cuda")
+    rc = L.af_rmsnorm_w8a16_gemv(xd.data_ptr(), gd.data_ptr(), EPS, qd.data_ptr(), sd.data_ptr(), y.data_ptr(), N, K,
+                                 128, 0, xn.data_ptr(), st())
+    assert rc == 0, L.af_status_string(rc)
+    xn_ref = ref_rmsnorm(xd, gd, K)
+    xn_b, xn_ref_b = host16(xn), host16(xn_ref)
+    diff = np.flatnonzero(xn_b != xn_ref_b)
+    assert diff.size == 0, f"x_norm differs from the reference rms_norm at {diff.size} of {K}: {diff[:8]}"
+    y_unfused = gemv(xn_ref, qd, sd, N, K)
+    assert np.array_equal(host16(y), host16(y_unfused))
+    check_gemv(host16(y), xn_ref_b[None, :], q, s, f"rmsnorm+gemv {N}x{K}")
+
+
+@pytest.mark.parametrize("N,K", [(3072, 3072), (3072, 8192), (1000, 1024)])
+def test_gemv_residual(N, K):
+    L = lib()
+    x, q, s = make_gemv_case(N + 3, 1, N, K)
+    res = fp16_bits(normal_f32(N + 5, (N,), 2.0))
+    xd, qd, sd = dev(x), dev(q), dev(s)
+    inout = dev(res.copy())
+    y_pre = torch.zeros(N, dtype=torch.int16, device="cuda")
+    rc = L.af_w8a16_gemv_residual(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), inout.data_ptr(), N, K, 128, 0,
+                                  y_pre.data_ptr(), st())
+    assert rc == 0, L.af_status_string(rc)
+    y_b = host16(y_pre)
+    assert np.array_equal(y_b, host16(gemv(xd, qd, sd, N, K)))
+    check_gemv(y_b, x, q, s, f"residual gemv {N}x{K}")
+    want = (res.view(np.float16).astype(np.float32) + y_b.view(np.float16).astype(np.float32)).astype(np.float16)
+    assert np.array_equal(host16(inout), want.view(np.uint16))
+    # the reference's residual add on the same operands agrees bit for bit
+    again = dev(res.copy())
+    assert ref().afref_residual_add(again.data_ptr(), y_pre.data_ptr(), N, st()) == 0
+    assert np.array_equal(host16(again), host16(inout))
+
+
+@pytest.mark.parametrize("N,K,with_norm", [(8192, 3072, True), (8192, 3072, False), (1000, 1024, True)])
+def test_rmsnorm_swiglu(N, K, with_norm):
+    L = lib()
+    x, gam = norm_inputs(N + K + 1, K, 1.0)
+    _, qg, sg = make_gemv_case(N + 11, 1, N, K)
+    _, qu, su = make_gemv_case(N + 13, 1, N, K)
+    xd, gd = dev(x), dev(gam)
+    qgd, sgd, qud, sud = dev(qg), dev(sg), dev(qu), dev(su)
+    h = torch.zeros(N, dtype=torch.int16, device="cuda")
+    gu = torch.zeros(2 * N, dtype=torch.int16, device="cuda")
+    xn = torch.zeros(K, dtype=torch.int16, device="cuda")
+    rc = L.af_rmsnorm_w8a16_swiglu(xd.data_ptr(), gd.data_ptr() if with_norm else None, EPS, qgd.data_ptr(),
+                                   sgd.data_ptr(), qud.data_ptr(), sud.data_ptr(), h.data_ptr(), N, K, 128, 0,
+                                   gu.data_ptr(), xn.data_ptr() if with_norm else None, st())
+    assert rc == 0, L.af_status_string(rc)
+    if with_norm:
+        xin = host16(xn)
+        assert np.array_equal(xin, host16(ref_rmsnorm(xd, gd, K)))
+    else:
+        xin = x.reshape(-1)
+    gu_b = host16(gu)
+    check_gemv(gu_b[:N], xin[None, :], qg, sg, f"gate {N}x{K}")
+    check_gemv(gu_b[N:], xin[None, :], qu, su, f"up {N}x{K}")
+    h_ref = torch.zeros(N, dtype=torch.int16, device="cuda")
+    assert ref().afref_swiglu(gu[:N].data_ptr(), gu[N:].data_ptr(), h_ref.data_ptr(), N, st()) == 0
+    hb, hrb = host16(h), host16(h_ref)
+    diff = np.flatnonzero(hb != hrb)
+    assert diff.size == 0, f"SwiGLU differs from the reference at {diff.size} of {N}: {diff[:8]}"
+
+
+def test_fused_graph_replay_is_stable():
+    """Graph-captured fused layer ops give the same bits on every replay."""
+    L = lib()
+    N, K = 3072, 3072
+    x, gam = norm_inputs(5, K, 1.0)
+    _, q, s = make_gemv_case(6, 1, N, K)
+    xd, gd, qd, sd = dev(x), dev(gam), dev(q), dev(s)
+    y = torch.zeros(N, dtype=torch.int16, device="cuda")
+    res0 = dev(fp16_bits(normal_f32(8, (N,), 1.0)))
+    inout = res0.clone()
+    stream = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        assert L.af_rmsnorm_w8a16_gemv(xd.data_ptr(), gd.data_ptr(), EPS, qd.data_ptr(), sd.data_ptr(), y.data_ptr(),
+                                       N, K, 128, 0, None, stream.cuda_stream) == 0
+    stream.synchronize()
+    with torch.cuda.graph(g, stream=stream):
+        inout.copy_(res0)
+        assert L.af_rmsnorm_w8a16_gemv(xd.data_ptr(), gd.data_ptr(), EPS, qd.data_ptr(), sd.data_ptr(), y.data_ptr(),
+                                       N, K, 128, 0, None, stream.cuda_stream) == 0
+        assert L.af_w8a16_gemv_residual(y.data_ptr(), qd.data_ptr(), sd.data_ptr(), inout.data_ptr(), N, K, 128, 0,
+                                        None, stream.cuda_stream) == 0
+    outs = []
+    for _ in range(3):
+        g.replay()
+        outs.append(host16(inout).copy())
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+
+
+def test_fused_argument_errors():
+    L = lib()
+    good = torch.zeros(4096, dtype=torch.uint8, device="cuda").data_ptr()
+    # K not a multiple of 128, N <= 0, missing norm weight, row scales for SwiGLU
+    assert L.af_rmsnorm_w8a16_gemv(good, good, EPS, good, good, good, 64, 100, 128, 0, None, None) == 1
+    assert L.af_w8a16_gemv_residual(good, good, good, good, 0, 128, 128, 0, None, None) == 1
+    assert L.af_rmsnorm_w8a16_gemv(good, None, EPS, good, good, good, 64, 128, 128, 0, None, None) == 1
+    assert L.af_rmsnorm_w8a16_swiglu(good, None, EPS, good, good, good, good, good, 64, 128, 128, 1, None, None,
+                                     None) == 2

@@ -69,6 +69,16 @@ def _rank_main(rank, world, port, out_q):
         for o in outs:
             assert_fp16_parity(o, ref, f"{name} rank {rank}")
         assert all(np.array_equal(outs[0], o) for o in outs[1:])
+        # the same all-reduce with the residual add folded in
+        res = (torch.randn(1, N, generator=g) * 2).half()
+        inout = res.cuda()
+        with torch.cuda.stream(st):
+            assert comm.L.af_w8a16_gemv_allreduce_residual(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(),
+                                                           inout.data_ptr(), N, K // world, 128, 0, comm.h,
+                                                           st.cuda_stream) == 0
+        st.synchronize()
+        want = (res.float() + torch.from_numpy(outs[0].view(np.float16).astype(np.float32))).half()
+        assert torch.equal(inout.cpu().view(torch.int16), want.view(torch.int16))
         results[name] = outs[0].tobytes()
     gathered = [None] * world
     dist.all_gather_object(gathered, results)

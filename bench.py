@@ -146,6 +146,124 @@ def make_layerset(device, rank, world, seed=1234):
     return items
 
 
+NORM_EPS = 1e-5
+
+
+def make_layerchain(device, rank, world, seed=1234):
+    """The decode layer without attention, in the reference's order
+    (src/core/engine.cu:292-483): RMSNorm -> QKV, O (input: the first K_o
+    entries of QKV, standing in for attention) -> residual, RMSNorm -> gate, up
+    -> SwiGLU -> down -> residual, for 28 layers of config-1 weights.  FP32 norm
+    weights 1 + N(0, 0.1); the residual stream x ~ N(0, 1) is reset every step."""
+    items = make_layerset(device, rank, world, seed)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed + 77)
+    layers = []
+    for l in range(NLAYERS):
+        p = {it["name"]: it for it in items[5 * l:5 * l + 5]}
+        for it in p.values():
+            it.pop("x", None)
+            it.pop("y", None)
+        layers.append(dict(p, layer=l, name=f"layer{l}", split="chain",
+                           g_attn=(1 + 0.1 * torch.randn(D, generator=g, device=device)).float().contiguous(),
+                           g_mlp=(1 + 0.1 * torch.randn(D, generator=g, device=device)).float().contiguous()))
+    qkv_n, ffn_n = layers[0]["qkv"]["N"], layers[0]["gate"]["N"]
+    bufs = dict(x0=torch.randn(1, D, generator=g, device=device).half(),
+                x=torch.zeros(1, D, dtype=torch.float16, device=device),
+                qkv=torch.zeros(1, qkv_n, dtype=torch.float16, device=device),
+                h=torch.zeros(1, ffn_n, dtype=torch.float16, device=device),
+                # reference arm intermediates (it stores every stage, as engine.cu does)
+                xn=torch.zeros(1, D, dtype=torch.float16, device=device),
+                o=torch.zeros(1, D, dtype=torch.float16, device=device),
+                up=torch.zeros(1, ffn_n, dtype=torch.float16, device=device))
+    return layers, bufs
+
+
+def chain_bytes(layers, tp):
+    """Algorithmic bytes of one step on one rank: every projection's weights,
+    scales and x/y, the norm weights and x, and the residual reads."""
+    b = 0
+    for ly in layers:
+        for nm in ("qkv", "o", "gate", "up", "down"):
+            b += algorithmic_bytes(ly[nm]["N"], ly[nm]["K"])
+        b += 2 * (D * 4 + D * 2)        # two RMSNorms: weight + x
+        b += 2 * D * 2                  # two residual reads
+    return b
+
+
+class OursChain:
+    """4 launches per layer: af_rmsnorm_w8a16_gemv (QKV), af_w8a16_gemv_residual
+    (O), af_rmsnorm_w8a16_swiglu (gate/up), af_w8a16_gemv_residual (down); at
+    N > 1 the row-split O/down are af_w8a16_gemv_allreduce_residual."""
+    launches_per_layer = 4
+
+    def __init__(self, bufs):
+        self.L = af_lib()
+        self.b = bufs
+        self.comm = None
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise RuntimeError(f"{what}: {self.L.af_status_string(rc).decode()}")
+
+    def _row(self, stream, it, xptr):
+        xo = self.b["x"].data_ptr()
+        if self.comm is not None:
+            self._check(self.L.af_w8a16_gemv_allreduce_residual(xptr, it["q"].data_ptr(), it["s"].data_ptr(), xo,
+                                                                 it["N"], it["K"], 128, 0, self.comm.h,
+                                                                 stream.cuda_stream), "allreduce_residual")
+        else:
+            self._check(self.L.af_w8a16_gemv_residual(xptr, it["q"].data_ptr(), it["s"].data_ptr(), xo, it["N"],
+                                                      it["K"], 128, 0, None, stream.cuda_stream), "gemv_residual")
+
+    def launch(self, stream, ly, xptr=None, yptr=None):
+        b, L, st = self.b, self.L, stream.cuda_stream
+        q = ly["qkv"]
+        self._check(L.af_rmsnorm_w8a16_gemv(b["x"].data_ptr(), ly["g_attn"].data_ptr(), NORM_EPS, q["q"].data_ptr(),
+                                            q["s"].data_ptr(), b["qkv"].data_ptr(), q["N"], q["K"], 128, 0, None,
+                                            st), "rmsnorm_gemv")
+        self._row(stream, ly["o"], b["qkv"].data_ptr())
+        ga, up = ly["gate"], ly["up"]
+        self._check(L.af_rmsnorm_w8a16_swiglu(b["x"].data_ptr(), ly["g_mlp"].data_ptr(), NORM_EPS, ga["q"].data_ptr(),
+                                              ga["s"].data_ptr(), up["q"].data_ptr(), up["s"].data_ptr(),
+                                              b["h"].data_ptr(), ga["N"], ga["K"], 128, 0, None, None, st),
+                    "rmsnorm_swiglu")
+        self._row(stream, ly["down"], b["h"].data_ptr())
+
+
+class RefChain:
+    """The reference's own kernels in engine.cu's order, 10 launches per layer:
+    rms_norm, gemv QKV, gemv O, residual_add, rms_norm, gemv gate, gemv up,
+    swiglu, gemv down, residual_add (oracle/_ref, compiled from its sources)."""
+    launches_per_layer = 10
+
+    def __init__(self, bufs):
+        import oracle
+        self.R = oracle.ref()
+        if self.R is None:
+            raise FileNotFoundError("oracle/_ref/libafref.so")
+        self.b = bufs
+
+    def launch(self, stream, ly, xptr=None, yptr=None):
+        R, b, st = self.R, self.b, stream.cuda_stream
+        x, xn, o, h, up = (b[k].data_ptr() for k in ("x", "xn", "o", "h", "up"))
+        rc = R.afref_rms_norm(x, ly["g_attn"].data_ptr(), xn, D, NORM_EPS, st)
+        q = ly["qkv"]
+        rc |= R.afref_w8a16_gemv(xn, q["q"].data_ptr(), q["s"].data_ptr(), b["qkv"].data_ptr(), q["N"], q["K"], st)
+        oo = ly["o"]
+        rc |= R.afref_w8a16_gemv(b["qkv"].data_ptr(), oo["q"].data_ptr(), oo["s"].data_ptr(), o, oo["N"], oo["K"], st)
+        rc |= R.afref_residual_add(x, o, D, st)
+        rc |= R.afref_rms_norm(x, ly["g_mlp"].data_ptr(), xn, D, NORM_EPS, st)
+        ga, uu, dd = ly["gate"], ly["up"], ly["down"]
+        rc |= R.afref_w8a16_gemv(xn, ga["q"].data_ptr(), ga["s"].data_ptr(), h, ga["N"], ga["K"], st)
+        rc |= R.afref_w8a16_gemv(xn, uu["q"].data_ptr(), uu["s"].data_ptr(), up, uu["N"], uu["K"], st)
+        rc |= R.afref_swiglu(h, up, h, ga["N"], st)
+        rc |= R.afref_w8a16_gemv(h, dd["q"].data_ptr(), dd["s"].data_ptr(), o, dd["N"], dd["K"], st)
+        rc |= R.afref_residual_add(x, o, D, st)
+        if rc != 0:
+            raise RuntimeError(f"reference chain launch failed ({rc})")
+
+
 def make_single(device, N, K, M, seed=99):
     """One GEMV shape, with enough rotating weight copies to exceed 4x L2."""
     copies = max(2, int(np.ceil(4 * 128e6 / (N * K))))
@@ -393,6 +511,14 @@ def main():
                   "weights_gb": round(sum(it["q"].numel() for it in items) * tp / 1e9, 3),
                   "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
                   "parallelism": f"tp{tp}" if tp > 1 else "single"}
+    elif wl == "layerchain":
+        items, cbufs = make_layerchain(device, trank, tp)
+        config = {"workload": "llama3.2-3b decode layer without attention x28 (RMSNorm, QKV, O + residual, "
+                              "RMSNorm, gate/up + SwiGLU, down + residual)", "M": 1,
+                  "attention": "out of scope: O reads the first K_o entries of QKV in its place",
+                  "scales": "fp16 per 128-group (reference format)", "layers": NLAYERS,
+                  "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
+                  "parallelism": f"tp{tp}" if tp > 1 else "single"}
     elif wl.startswith("gemv:"):
         parts = [int(v) for v in wl.split(":")[1:]]
         N, K = parts[0], parts[1]
@@ -411,20 +537,24 @@ def main():
         raise SystemExit(f"unknown workload {wl}")
 
     lm = wl.startswith("lmhead")
-    arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
+    chain = wl == "layerchain"
+    if chain:
+        arm = OursChain(cbufs) if args.impl == "ours" else None
+    else:
+        arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
     if args.impl == "reference":
         try:
             if lm and wl.endswith("fp8"):
                 raise FileNotFoundError("an FP8 lm_head (the reference's lm_head is FP16 cuBLAS only)")
-            arm = RefLmHead(items, device) if lm else RefGemv(items, device)
+            arm = RefChain(cbufs) if chain else (RefLmHead(items, device) if lm else RefGemv(items, device))
         except FileNotFoundError as e:
             print(json.dumps({"impl": "reference", "unavailable": f"no reference arm: {e}"}))
             return 0
     stream = torch.cuda.Stream(device)
     allreduce = None
     comm = None
-    if tp > 1 and wl.startswith("lmhead") and args.tp_comm == "nccl":
-        raise SystemExit("vocab-parallel lm_head exchanges its argmax inside the kernel (--tp-comm fused)")
+    if tp > 1 and (lm or chain) and args.tp_comm == "nccl":
+        raise SystemExit("the lm_head and layer-chain workloads exchange inside their kernels (--tp-comm fused)")
     if tp > 1 and args.tp_comm == "nccl":
         def allreduce(y):
             torch.distributed.all_reduce(y)
@@ -432,24 +562,38 @@ def main():
         # row-split projections: one kernel computes the partial GEMV and sums it
         # over the ranks through NVLink peer memory (af_w8a16_gemv_allreduce)
         from atomflow_b200.tp import TpComm
-        comm = TpComm(trank, tp, max(it["N"] for it in items) if not wl.startswith("lmhead") else 64)
+        comm = TpComm(trank, tp, D if chain else (max(it["N"] for it in items) if not lm else 64))
         arm.comm = comm
 
-    step_bytes = (sum(lm_bytes(it) for it in items) if lm else
+    step_bytes = (sum(lm_bytes(it) for it in items) if lm else chain_bytes(items, tp) if chain else
                   sum(algorithmic_bytes(it["N"], it["K"], it["x"].shape[0]) for it in items))
     total_bytes = step_bytes * tp
     sampler = ClockSampler(local) if rank == 0 else None
-    g = capture_step(arm, items, stream, allreduce)
+    reset = (lambda: cbufs["x"].copy_(cbufs["x0"])) if chain else None
+    g = capture_step(arm, items, stream, allreduce, pre=reset)
     if sampler:
         sampler.wait_first()
     ms, t0, t1 = time_graph(g, stream, args.steps, args.warmup, dist_on)
     clocks = sampler.summary(t0, t1) if sampler else None
     ms_step = ms / args.steps
     value = total_bytes / (ms_step / 1e3) / 1e9
-    launches = len(items) * args.steps
+    launches = len(items) * args.steps * (arm.launches_per_layer if chain else 1)
 
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and chain:
+        # End to end through the C ABI: each step takes the residual stream from
+        # pinned host memory and returns it there (a decode step's real I/O).
+        x_host = cbufs["x0"].cpu().pin_memory()
+        x_back = torch.empty_like(x_host).pin_memory()
+        ge = capture_step(arm, items, stream, allreduce, lambda: cbufs["x"].copy_(x_host, non_blocking=True),
+                          lambda: x_back.copy_(cbufs["x"], non_blocking=True))
+        ems, _, _ = time_graph(ge, stream, args.steps, args.warmup, dist_on)
+        e2e = {"value": round(total_bytes / (ems / args.steps / 1e3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(ems / args.steps, 5), "h2d_bytes_per_step": int(x_host.numel() * 2),
+               "d2h_bytes_per_step": int(x_back.numel() * 2),
+               "path": "af_rmsnorm_w8a16_gemv / af_w8a16_gemv_residual / af_rmsnorm_w8a16_swiglu C ABI; residual "
+                       "stream pinned host -> device -> pinned host each step; CUDA graph"}
+    elif not args.no_e2e:
         # End to end through the C ABI with host buffers: every step copies all
         # 140 activation vectors from pinned host memory, runs the GEMVs and
         # copies every output back; graph-captured like the reference's decode.
@@ -503,6 +647,7 @@ def main():
     per_rank_gbs = step_bytes / (ms_step / 1e3) / 1e9
     out = {
         "metric": ("lm_head vocab projection + argmax achieved HBM GB/s" if lm else
+                   "decode-layer chain achieved HBM GB/s (Llama-3.2-3B, M=1, attention excluded)" if chain else
                    "W8A16 GEMV achieved HBM GB/s (Llama-3.2-3B layer-set stream, M=1)"),
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
@@ -516,8 +661,9 @@ def main():
                      "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
                                  "reference": "cublasGemmEx + argmax (reference)"} if lm else
                                 {"ours": "gemv_fp8_m1_kernel", "reference": "w8a16_gemv_kernel (reference)"})[args.impl],
-                     "per_launch": f"{step_bytes / len(items) / 1e6:.2f} MB avg algorithmic bytes / launch over "
-                                   f"{ms_step * 1e3 / len(items):.2f} us avg launch (CUDA events over the timed region)"},
+                     "per_launch": f"{step_bytes / (launches / args.steps) / 1e6:.2f} MB avg algorithmic bytes / launch "
+                                   f"over {ms_step * 1e3 / (launches / args.steps):.2f} us avg launch (CUDA events "
+                                   f"over the timed region)"},
         "gpu_launches": launches if args.impl == "ours" else 0,
         "clocks": clocks,
     }

@@ -126,13 +126,13 @@ def algorithmic_bytes(N, K, M=1, scale="group"):
 
 # --------------------------------------------------------------- workload
 
-def make_layerset(device, rank, world, seed=1234):
+def make_layerset(device, rank, world, seed=1234, layers=NLAYERS):
     """Config-1 weights: per (layer, projection) W ~ N(0, 0.02) quantised to E4M3
     with FP16 group scales (the reference's format); x ~ N(0, 1) FP16.  Under TP
     each rank keeps its shard of every projection."""
     items = []
     g = torch.Generator(device=device)
-    for layer in range(NLAYERS):
+    for layer in range(layers):
         for pi, (name, N, K, split) in enumerate(PROJ):
             g.manual_seed(seed + 1000 * layer + pi)
             w = torch.randn(N, K, generator=g, device=device, dtype=torch.float32) * 0.02
@@ -149,17 +149,17 @@ def make_layerset(device, rank, world, seed=1234):
 NORM_EPS = 1e-5
 
 
-def make_layerchain(device, rank, world, seed=1234):
+def make_layerchain(device, rank, world, seed=1234, layers=NLAYERS):
     """The decode layer without attention, in the reference's order
     (src/core/engine.cu:292-483): RMSNorm -> QKV, O (input: the first K_o
     entries of QKV, standing in for attention) -> residual, RMSNorm -> gate, up
     -> SwiGLU -> down -> residual, for 28 layers of config-1 weights.  FP32 norm
     weights 1 + N(0, 0.1); the residual stream x ~ N(0, 1) is reset every step."""
-    items = make_layerset(device, rank, world, seed)
+    items = make_layerset(device, rank, world, seed, layers)
     g = torch.Generator(device=device)
     g.manual_seed(seed + 77)
-    layers = []
-    for l in range(NLAYERS):
+    nlayers, layers = layers, []
+    for l in range(nlayers):
         p = {it["name"]: it for it in items[5 * l:5 * l + 5]}
         for it in p.values():
             it.pop("x", None)
@@ -484,6 +484,8 @@ def main():
     ap.add_argument("--workload", default="layerset")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=NLAYERS,
+                    help="layers of the layerset / layerchain workloads (default 28; fewer only for profiling)")
     ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",
                     help="N > 1: all-reduce of row-split outputs inside the GEMV kernel (fused) or by NCCL")
     args = ap.parse_args()
@@ -504,19 +506,19 @@ def main():
 
     wl = args.workload
     if wl == "layerset":
-        items = make_layerset(device, trank, tp)
-        config = {"workload": "llama3.2-3b layer-set x28 (BASELINE config 1)", "M": 1,
+        items = make_layerset(device, trank, tp, layers=args.layers)
+        config = {"workload": f"llama3.2-3b layer-set x{args.layers} (BASELINE config 1)", "M": 1,
                   "shapes": "qkv 5120x3072, o 3072x3072, gate/up 8192x3072, down 3072x8192",
                   "scales": "fp16 per 128-group (reference format)", "gemvs_per_step": len(items),
                   "weights_gb": round(sum(it["q"].numel() for it in items) * tp / 1e9, 3),
                   "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
                   "parallelism": f"tp{tp}" if tp > 1 else "single"}
     elif wl == "layerchain":
-        items, cbufs = make_layerchain(device, trank, tp)
-        config = {"workload": "llama3.2-3b decode layer without attention x28 (RMSNorm, QKV, O + residual, "
+        items, cbufs = make_layerchain(device, trank, tp, layers=args.layers)
+        config = {"workload": f"llama3.2-3b decode layer without attention x{args.layers} (RMSNorm, QKV, O + residual, "
                               "RMSNorm, gate/up + SwiGLU, down + residual)", "M": 1,
                   "attention": "out of scope: O reads the first K_o entries of QKV in its place",
-                  "scales": "fp16 per 128-group (reference format)", "layers": NLAYERS,
+                  "scales": "fp16 per 128-group (reference format)", "layers": args.layers,
                   "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
                   "parallelism": f"tp{tp}" if tp > 1 else "single"}
     elif wl.startswith("gemv:"):

@@ -501,7 +501,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 //   * PAIR (gate/up + SwiGLU): a 16-row MMA tile holds 8 gate rows and the same
 //     8 up rows, so each lane owns gate[r] and up[r] and applies the
 //     activation in registers.
-template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas, bool PAIR>
+//   * MT = 8 (2..8 tokens): the MMA's 8 columns carry 8 tokens -- lane (g, c)
+//     feeds token g's x -- so a batch costs the MMA instructions of one token;
+//     x rows sit in shared memory 16 bytes apart modulo 128 (bank-conflict free).
+template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas, bool PAIR, int MT = 1>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
@@ -617,14 +620,21 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     // x may be written by the kernel this one waits for, so it is read only
     // after the wait; an L2 prefetch now is only a hint (L2 is the point of
     // coherence) and turns that read into an L2 hit when x was not just written.
-    if (threadIdx.x == 32) bulk_prefetch_l2(p.x, (uint32_t)p.K * 2u);
+    if (threadIdx.x == 32) bulk_prefetch_l2(p.x, (uint32_t)p.M * p.K * 2u);
 
     pdl_wait();
     TRACE(1);
     // x by one bulk copy on the TMA engine (see above)
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.K * 2u);
-        bulk_g2s(smem_u32(xs), p.x, (uint32_t)p.K * 2u, smem_u32(&s_xbar));
+        if (MT == 1) {
+            mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.K * 2u);
+            bulk_g2s(smem_u32(xs), p.x, (uint32_t)p.K * 2u, smem_u32(&s_xbar));
+        } else {
+            mbar_arrive_expect_tx(smem_u32(&s_xbar), (uint32_t)p.M * p.K * 2u);
+            for (int m = 0; m < p.M; ++m)
+                bulk_g2s(smem_u32(xs + (size_t)m * p.xs_stride), p.x + (size_t)m * p.K, (uint32_t)p.K * 2u,
+                         smem_u32(&s_xbar));
+        }
     }
     __shared__ unsigned s_ep;   // this launch's epoch (tensor-parallel epilogue)
     if (p.tp_world > 1 && threadIdx.x == 0)
@@ -632,7 +642,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
     mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
-    if (p.norm_w != nullptr) {
+    if (MT == 1 && p.norm_w != nullptr) {
         // RMSNorm of x in place, in the reference's arithmetic order
         // (src/kernel/rmsnorm.cu:9-67, 128 threads): per-thread strided FMA
         // sums, each warp's shuffle-down tree, the warps' sums in order, then
@@ -666,7 +676,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
 
     // ---- compute cursor ----
     const unsigned char* my_ring_p = ring + (size_t)warp * kS * kSlot + lane * 16;
-    const __half* my_x = xs + c * (16 / ESZ);
+    // MT = 8: lane (g, c) feeds token g (tokens >= M read zeros)
+    const bool x_on = MT == 1 || g < p.M;
+    const __half* my_x = xs + (MT == 1 ? 0 : (size_t)(x_on ? g : 0) * p.xs_stride) + c * (16 / ESZ);
     const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
     const float* rs = static_cast<const float*>(p.s);
     int c_tile = wc0 / (cpt > 0 ? cpt : 1);
@@ -707,6 +719,30 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     int best_i = -1;
 
     auto emit = [&](int tile, const float (&v)[4]) {
+        if (MT > 1) {
+            // lane (g, c) holds rows g, g+8 for tokens 2c, 2c+1
+            const int r0 = row0 + tile * 16 + g, r1 = r0 + 8;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int tok = 2 * c + j;
+                if (tok >= p.M) continue;
+                float a = v[j], b = v[2 + j];
+                if (!GROUP && rs != nullptr) {
+                    a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
+                    b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
+                }
+                if (p.y_f32) {
+                    float* yo = static_cast<float*>(p.y) + (size_t)tok * p.N;
+                    if (r0 < row1) yo[r0] = a;
+                    if (r1 < row1) yo[r1] = b;
+                } else {
+                    __half* yo = static_cast<__half*>(p.y) + (size_t)tok * p.N;
+                    if (r0 < row1) yo[r0] = __float2half_rn(a);
+                    if (r1 < row1) yo[r1] = __float2half_rn(b);
+                }
+            }
+            return;
+        }
         if (c != 0) return;   // token 0 sits in MMA column 0 (lanes c == 0)
         const int r0 = row0 + tile * TR + g, r1 = r0 + 8;
         float a = v[0], b = v[2];
@@ -792,6 +828,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             xv[2] = *reinterpret_cast<const uint4*>(xp_ + 64);
             xv[3] = *reinterpret_cast<const uint4*>(xp_ + 72);
         }
+        if (MT > 1 && !x_on) xv[0] = xv[1] = xv[2] = xv[3] = make_uint4(0, 0, 0, 0);
         float s0 = 1.f, s1 = 1.f;
         if (GROUP) {
             s0 = half_bits_to_float(sp0[c_kc]);
@@ -1136,10 +1173,10 @@ cudaError_t launch_stream(const GemvParams& prm, const Plan& pl, size_t smem, cu
     return launch_pdl(kern, dim3(pl.grid), dim3(kWarpsPerCta * 32), smem, st, prm);
 }
 
-template <bool GROUP, bool F16, int NW, int NS, bool PAIR = false>
+template <bool GROUP, bool F16, int NW, int NS, bool PAIR = false, int MT = 1>
 cudaError_t launch_m1(const GemvParams& prm, const Plan& pl, size_t smem, cudaStream_t st) {
     // a ring past ~100 KB means one CTA per SM: registers may grow
-    auto kern = gemv_fp8_m1_kernel<GROUP, F16, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2), PAIR>;
+    auto kern = gemv_fp8_m1_kernel<GROUP, F16, NW, NS, (NW * NS * 2 > 100) ? 1 : (NW <= 6 ? 3 : 2), PAIR, MT>;
     static std::once_flag flags[kMaxDevices];
     static cudaError_t attr_err[kMaxDevices];
     int dev = 0;
@@ -1260,6 +1297,31 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         if (ring + slots + sc > budget || sc > 32 * 1024) sc = 0;
     }
     const size_t gam = (fz != nullptr && fz->norm_w != nullptr) ? round_up((size_t)K * 4, 128) : 0;
+    // 2..8 tokens: the one-token kernel with the tokens in the MMA's columns.
+    if (M >= 2 && M <= 8 && fz == nullptr && tp == nullptr && arg_out == nullptr && wk != W_F16 &&
+        K % 128 == 0 && aligned(x, 16) && m1_enabled()) {
+        const size_t stride = (size_t)K + 8;   // halves: token rows 16 B apart modulo 128
+        const size_t xs1 = round_up((size_t)M * stride * 2, 128);
+        const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
+        struct Opt { int ns; size_t cap; };
+        const Opt opts[4] = {{5, 113 * 1024}, {3, 113 * 1024}, {5, kSmemMax - 1024}, {3, kSmemMax - 1024}};
+        for (const Opt& o : opts) {
+            for (size_t scx : {sc1, (size_t)0}) {
+                const size_t smem1 = (size_t)8 * o.ns * 2048 + xs1 + scx;
+                if (smem1 > o.cap) continue;
+                prm.xs_stride = (int)stride;
+                prm.pre = m1_pre(o.ns);
+                prm.xs_bytes = (int)xs1;
+                prm.sc_bytes = (int)scx;
+                cudaError_t e;
+#define AF_MT(NS) (wk == W_FP8_GROUP ? launch_m1<true, false, 8, NS, false, 8>(prm, pl, smem1, st) \
+                                    : launch_m1<false, false, 8, NS, false, 8>(prm, pl, smem1, st))
+                e = o.ns == 5 ? AF_MT(5) : AF_MT(3);
+#undef AF_MT
+                return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_fp8_m1_kernel (tokens in MMA columns)");
+            }
+        }
+    }
     // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
     // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
     if (M == 1 && (wk == W_F16 ? K % 64 : K % 128) == 0 && aligned(x, 16) && m1_enabled()) {

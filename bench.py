@@ -343,10 +343,15 @@ class RefGemv:
         self.items = items
 
     def launch(self, stream, it, xptr=None, yptr=None):
-        rc = self.L.afref_w8a16_gemv(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
-                                     yptr or it["y"].data_ptr(), it["N"], it["K"], stream.cuda_stream)
-        if rc != 0:
-            raise RuntimeError(f"reference launch failed ({rc})")
+        # The reference kernel computes one token per launch (qkv_gemm.cu:129-150 ignores M),
+        # so M tokens are M launches, one per row of x and y.
+        M, K, N = it["x"].shape[0], it["K"], it["N"]
+        x0, y0 = xptr or it["x"].data_ptr(), yptr or it["y"].data_ptr()
+        for m in range(M):
+            rc = self.L.afref_w8a16_gemv(x0 + m * K * 2, it["q"].data_ptr(), it["s"].data_ptr(), y0 + m * N * 2, N, K,
+                                         stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"reference launch failed ({rc})")
 
 
 class OursLmHead:
@@ -679,7 +684,7 @@ def main():
         out["cpu_baseline"] = {"value": out["value"], "unit": "GB/s", "cores": None, "kind": "reference",
                                "sample": "full workload; the reference's path is CUDA (src/kernel/qkv_gemm.cu "
                                          "w8a16_gemv_kernel, compiled from its sources), run on this GPU"}
-        out["reference_kernel_launches"] = launches
+        out["reference_kernel_launches"] = launches * (items[0]["x"].shape[0] if wl.startswith("gemv:") else 1)
     print(json.dumps(out))
     finish(dist_on)
 

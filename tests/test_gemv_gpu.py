@@ -89,7 +89,8 @@ def test_gemv_batched_tokens(M, N, K):
 
 
 @pytest.mark.parametrize("kind", ["row", "none"])
-@pytest.mark.parametrize("M,N,K", [(1, 3072, 3072), (1, 8192, 3072), (5, 777, 192), (16, 512, 4096)])
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 3072), (1, 8192, 3072), (5, 777, 192), (16, 512, 4096),
+                                   (4, 1000, 1024), (8, 3072, 8192)])
 def test_gemv_row_scale_and_unscaled(kind, M, N, K):
     x, q, s = make_gemv_case(31 + M + N, M, N, K, kind=kind)
     y = gemv_np(x, q, s, kind)

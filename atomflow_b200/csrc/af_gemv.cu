@@ -504,10 +504,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 //   * MT = 8 (2..8 tokens): the MMA's 8 columns carry 8 tokens -- lane (g, c)
 //     feeds token g's x -- so a batch costs the MMA instructions of one token;
 //     x rows sit in shared memory 16 bytes apart modulo 128 (bank-conflict free).
+//     MT = 16 (9..16 tokens): a second MMA per k-step on the same converted
+//     weights for tokens 8..15.
 template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas, bool PAIR, int MT = 1>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
+    constexpr int NQ = MT == 16 ? 8 : 4;   // accumulators per lane
 #ifdef AF_EXP_TRACE
     __shared__ unsigned s_tl;
     if (threadIdx.x == 0) s_tl = atomicAdd(&g_trace_launch, 1) / gridDim.x;
@@ -679,6 +682,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     // MT = 8: lane (g, c) feeds token g (tokens >= M read zeros)
     const bool x_on = MT == 1 || g < p.M;
     const __half* my_x = xs + (MT == 1 ? 0 : (size_t)(x_on ? g : 0) * p.xs_stride) + c * (16 / ESZ);
+    const bool x_on1 = MT == 16 && g + 8 < p.M;   // second token group (MT = 16)
+    const __half* my_x1 = xs + (MT == 16 ? (size_t)(x_on1 ? g + 8 : 0) * p.xs_stride : 0) + c * (16 / ESZ);
     const uint16_t* s16 = static_cast<const uint16_t*>(p.s);
     const float* rs = static_cast<const float*>(p.s);
     int c_tile = wc0 / (cpt > 0 ? cpt : 1);
@@ -712,21 +717,22 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     };
     c_rows();
 
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    float part0[4] = {0.f, 0.f, 0.f, 0.f}, part1[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[NQ], part0[NQ], part1[NQ];
+#pragma unroll
+    for (int k = 0; k < NQ; ++k) acc[k] = part0[k] = part1[k] = 0.f;
     const int first_tile = wc0 < wc1 ? c_tile : -1;
     float best_v = 0.f;
     int best_i = -1;
 
-    auto emit = [&](int tile, const float (&v)[4]) {
+    auto emit = [&](int tile, const float (&v)[NQ]) {
         if (MT > 1) {
-            // lane (g, c) holds rows g, g+8 for tokens 2c, 2c+1
+            // lane (g, c) holds rows g, g+8 for tokens 2c, 2c+1 (and 8+2c, 9+2c)
             const int r0 = row0 + tile * 16 + g, r1 = r0 + 8;
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const int tok = 2 * c + j;
+            for (int j = 0; j < NQ / 2; ++j) {
+                const int tok = (j >> 1) * 8 + 2 * c + (j & 1);
                 if (tok >= p.M) continue;
-                float a = v[j], b = v[2 + j];
+                float a = v[(j >> 1) * 4 + (j & 1)], b = v[(j >> 1) * 4 + 2 + (j & 1)];
                 if (!GROUP && rs != nullptr) {
                     a *= r0 < row1 ? __ldg(rs + r0) : 0.f;
                     b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
@@ -829,13 +835,24 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             xv[3] = *reinterpret_cast<const uint4*>(xp_ + 72);
         }
         if (MT > 1 && !x_on) xv[0] = xv[1] = xv[2] = xv[3] = make_uint4(0, 0, 0, 0);
+        uint4 xw[4];   // tokens 8..15 (MT = 16)
+        if (MT == 16) {
+            const __half* xq = my_x1 + c_kc * CPOS;
+            xw[0] = *reinterpret_cast<const uint4*>(xq);
+            xw[1] = *reinterpret_cast<const uint4*>(xq + 8);
+            xw[2] = *reinterpret_cast<const uint4*>(xq + 64);
+            xw[3] = *reinterpret_cast<const uint4*>(xq + 72);
+            if (!x_on1) xw[0] = xw[1] = xw[2] = xw[3] = make_uint4(0, 0, 0, 0);
+        }
         float s0 = 1.f, s1 = 1.f;
         if (GROUP) {
             s0 = half_bits_to_float(sp0[c_kc]);
             s1 = half_bits_to_float(sp1[c_kc]);
         }
         issue();   // this slot's bytes are in registers: refill it
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        float d[NQ];
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) d[k] = 0.f;
         // lane (g, c): bytes 4t..4t+3 of its 32 row bytes are MMA k-step t; its
         // x halves are in the same order, so the permutation of k cancels
 #pragma unroll
@@ -857,11 +874,15 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             mma16816(e, a0, a1, a2, a3, u4w(xv[t >> 1], (t & 1) * 2), u4w(xv[t >> 1], (t & 1) * 2 + 1));
 #pragma unroll
             for (int k = 0; k < 4; ++k) d[k] += e[k];
+            if (MT == 16) {
+                float e1[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(e1, a0, a1, a2, a3, u4w(xw[t >> 1], (t & 1) * 2), u4w(xw[t >> 1], (t & 1) * 2 + 1));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) d[4 + k] += e1[k];
+            }
         }
-        acc[0] = fmaf(s0, d[0], acc[0]);
-        acc[1] = fmaf(s0, d[1], acc[1]);
-        acc[2] = fmaf(s1, d[2], acc[2]);
-        acc[3] = fmaf(s1, d[3], acc[3]);
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) acc[k] = fmaf((k & 2) ? s1 : s0, d[k], acc[k]);
         if (++c_slot == kS) c_slot = 0;
         const bool tile_done = ++c_kc == cpt;
         if (j + 1 == wc1 || tile_done) {
@@ -869,12 +890,11 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                 emit(c_tile, acc);
             } else {
                 float* dst = c_tile == first_tile ? part0 : part1;   // registers until the ring is free
-                dst[0] = acc[0];
-                dst[1] = acc[1];
-                dst[2] = acc[2];
-                dst[3] = acc[3];
+#pragma unroll
+                for (int k = 0; k < NQ; ++k) dst[k] = acc[k];
             }
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+            for (int k = 0; k < NQ; ++k) acc[k] = 0.f;
             seg_lo = j + 1;
         }
         if (tile_done) {
@@ -886,10 +906,13 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     cp_async_wait<0>();
     TRACE(3);
     __syncthreads();   // every warp is done with the ring
-    *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 0) * 32 + lane) * 4) =
-        make_float4(part0[0], part0[1], part0[2], part0[3]);
-    *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 1) * 32 + lane) * 4) =
-        make_float4(part1[0], part1[1], part1[2], part1[3]);
+#pragma unroll
+    for (int q = 0; q < NQ / 4; ++q) {
+        *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 0) * 32 + lane) * NQ + 4 * q) =
+            make_float4(part0[4 * q], part0[4 * q + 1], part0[4 * q + 2], part0[4 * q + 3]);
+        *reinterpret_cast<float4*>(wslots + ((size_t)(warp * 2 + 1) * 32 + lane) * NQ + 4 * q) =
+            make_float4(part1[4 * q], part1[4 * q + 1], part1[4 * q + 2], part1[4 * q + 3]);
+    }
     __syncthreads();
     TRACE(4);
 
@@ -897,18 +920,24 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     // owners come from the warp-start table (no divisions on this serial tail).
     for (int t = warp; t < T; t += kWarps) {
         const int lo = t * cpt, hi = lo + cpt;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        float v[NQ];
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) v[k] = 0.f;
         int owners = 0;
         for (int w = 0; w < kWarps; ++w) {
             const int a = s_wstart[w], b = s_wstart[w + 1];
             if (a >= b || a >= hi || b <= lo) continue;
             ++owners;
             const int slot = a >= lo ? 0 : 1;   // t is w's first tile -> part0
-            const float4 f = *reinterpret_cast<const float4*>(wslots + ((size_t)(w * 2 + slot) * 32 + lane) * 4);
-            v[0] += f.x;
-            v[1] += f.y;
-            v[2] += f.z;
-            v[3] += f.w;
+#pragma unroll
+            for (int q = 0; q < NQ / 4; ++q) {
+                const float4 f =
+                    *reinterpret_cast<const float4*>(wslots + ((size_t)(w * 2 + slot) * 32 + lane) * NQ + 4 * q);
+                v[4 * q] += f.x;
+                v[4 * q + 1] += f.y;
+                v[4 * q + 2] += f.z;
+                v[4 * q + 3] += f.w;
+            }
         }
         if (owners < 2) continue;   // one owner: emitted from the main loop
         emit(t, v);
@@ -1143,6 +1172,15 @@ int m1_pre(int ns) {
     return (v < 0 || v > ns) ? ns : v;
 }
 
+// AF_M1_MT16=0 routes 9..16 tokens through the general kernel (A/B runs).
+bool mt16_enabled() {
+    static bool v = [] {
+        const char* e = getenv("AF_M1_MT16");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 // AF_M1_KERNEL=0 routes one-token FP8 GEMVs through the general kernel (for A/B runs).
 bool m1_enabled() {
     static bool v = [] {
@@ -1298,8 +1336,8 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     }
     const size_t gam = (fz != nullptr && fz->norm_w != nullptr) ? round_up((size_t)K * 4, 128) : 0;
     // 2..8 tokens: the one-token kernel with the tokens in the MMA's columns.
-    if (M >= 2 && M <= 8 && fz == nullptr && tp == nullptr && arg_out == nullptr && wk != W_F16 &&
-        K % 128 == 0 && aligned(x, 16) && m1_enabled()) {
+    if (M >= 2 && M <= 16 && fz == nullptr && tp == nullptr && arg_out == nullptr && wk != W_F16 &&
+        K % 128 == 0 && aligned(x, 16) && m1_enabled() && (M <= 8 || mt16_enabled())) {
         const size_t stride = (size_t)K + 8;   // halves: token rows 16 B apart modulo 128
         const size_t xs1 = round_up((size_t)M * stride * 2, 128);
         const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
@@ -1314,9 +1352,10 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
                 prm.xs_bytes = (int)xs1;
                 prm.sc_bytes = (int)scx;
                 cudaError_t e;
-#define AF_MT(NS) (wk == W_FP8_GROUP ? launch_m1<true, false, 8, NS, false, 8>(prm, pl, smem1, st) \
-                                    : launch_m1<false, false, 8, NS, false, 8>(prm, pl, smem1, st))
-                e = o.ns == 5 ? AF_MT(5) : AF_MT(3);
+#define AF_MT(NS, T) (wk == W_FP8_GROUP ? launch_m1<true, false, 8, NS, false, T>(prm, pl, smem1, st) \
+                                       : launch_m1<false, false, 8, NS, false, T>(prm, pl, smem1, st))
+                if (M > 8) e = o.ns == 5 ? AF_MT(5, 16) : AF_MT(3, 16);
+                else e = o.ns == 5 ? AF_MT(5, 8) : AF_MT(3, 8);
 #undef AF_MT
                 return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_fp8_m1_kernel (tokens in MMA columns)");
             }

@@ -1,7 +1,7 @@
 """Benchmark of the W8A16 decode hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload layerset|gemv:N:K[:M]|lmhead:f16|lmhead:fp8]
+                    [--workload layerset|layerset8b|layerchain|gemv:N:K[:M]|lmhead:f16|lmhead:fp8]
 
 Default workload: the Llama-3.2-3B-shaped projection set
 at M = 1 -- fused QKV [5120x3072], O [3072x3072], gate and up [8192x3072],
@@ -48,6 +48,10 @@ D, FFN, QKV = 3072, 8192, 5120
 NLAYERS = 28
 PROJ = [("qkv", QKV, D, "col"), ("o", D, D, "row"), ("gate", FFN, D, "col"),
         ("up", FFN, D, "col"), ("down", D, FFN, "row")]
+# BASELINE config 4's 8B-shaped layer: hidden 4096, intermediate 14336, GQA 32 Q / 8 KV heads of 128
+D8, FFN8, QKV8, NLAYERS8 = 4096, 14336, 4096 + 2 * 8 * 128, 32
+PROJ8 = [("qkv", QKV8, D8, "col"), ("o", D8, D8, "row"), ("gate", FFN8, D8, "col"),
+         ("up", FFN8, D8, "col"), ("down", D8, FFN8, "row")]
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -126,14 +130,14 @@ def algorithmic_bytes(N, K, M=1, scale="group"):
 
 # --------------------------------------------------------------- workload
 
-def make_layerset(device, rank, world, seed=1234, layers=NLAYERS):
+def make_layerset(device, rank, world, seed=1234, layers=NLAYERS, proj=PROJ):
     """Config-1 weights: per (layer, projection) W ~ N(0, 0.02) quantised to E4M3
     with FP16 group scales (the reference's format); x ~ N(0, 1) FP16.  Under TP
     each rank keeps its shard of every projection."""
     items = []
     g = torch.Generator(device=device)
     for layer in range(layers):
-        for pi, (name, N, K, split) in enumerate(PROJ):
+        for pi, (name, N, K, split) in enumerate(proj):
             g.manual_seed(seed + 1000 * layer + pi)
             w = torch.randn(N, K, generator=g, device=device, dtype=torch.float32) * 0.02
             x = torch.randn(1, K, generator=g, device=device, dtype=torch.float32).half()
@@ -518,6 +522,15 @@ def main():
                   "weights_gb": round(sum(it["q"].numel() for it in items) * tp / 1e9, 3),
                   "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
                   "parallelism": f"tp{tp}" if tp > 1 else "single"}
+    elif wl == "layerset8b":
+        nl = NLAYERS8 if args.layers == NLAYERS else args.layers
+        items = make_layerset(device, trank, tp, layers=nl, proj=PROJ8)
+        config = {"workload": f"llama3-8b-shaped layer-set x{nl} (BASELINE config 4, TP sharding)", "M": 1,
+                  "shapes": "qkv 6144x4096, o 4096x4096, gate/up 14336x4096, down 4096x14336",
+                  "scales": "fp16 per 128-group (reference format)", "gemvs_per_step": len(items),
+                  "weights_gb": round(sum(it["q"].numel() for it in items) * tp / 1e9, 3),
+                  "l2": "inputs >> 126 MB L2 (no flush needed)",
+                  "parallelism": f"tp{tp}" if tp > 1 else "single"}
     elif wl == "layerchain":
         items, cbufs = make_layerchain(device, trank, tp, layers=args.layers)
         config = {"workload": f"llama3.2-3b decode layer without attention x{args.layers} (RMSNorm, QKV, O + residual, "
@@ -655,6 +668,7 @@ def main():
     out = {
         "metric": ("lm_head vocab projection + argmax achieved HBM GB/s" if lm else
                    "decode-layer chain achieved HBM GB/s (Llama-3.2-3B, M=1, attention excluded)" if chain else
+                   "W8A16 GEMV achieved HBM GB/s (Llama-3-8B-shaped layer-set stream, M=1)" if wl == "layerset8b" else
                    "W8A16 GEMV achieved HBM GB/s (Llama-3.2-3B layer-set stream, M=1)"),
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,

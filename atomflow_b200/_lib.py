@@ -74,6 +74,14 @@ C_SYMBOLS = {
     "af_w8a16_gemv_residual": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "af_rmsnorm_w8a16_swiglu": (_i, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     "af_w8a16_gemv_allreduce_residual": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "af_embed_lookup": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "af_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float]),
+    "af_rope_kv_write": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "af_rope_set_form": (_i, [_i]),
+    "af_decode_attention_workspace_bytes": (_sz, [_i, _i]),
+    "af_decode_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "af_rmsnorm": (_i, [_vp, _vp, ctypes.c_float, _vp, _i, _vp]),
+    "af_decode_advance": (_i, [_vp, _i, _vp]),
     "af_view_last_status": (_i, []),
 }
 # C++ launchers with the reference's signatures (include/ops/kernel.h); references are pointers.

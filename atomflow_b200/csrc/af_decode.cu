@@ -1,0 +1,304 @@
+// af_decode.cu -- the rest of a decode step around the projections: token
+// embedding, RoPE + KV-cache write, cached GQA attention, standalone RMSNorm,
+// and the position counter.  Positions and tokens live in device memory, so a
+// whole autoregressive step (embedding .. argmax) replays as one CUDA graph.
+//
+// Reference counterparts: src/kernel/helpers.cu (k_embed_lookup_kernel,
+// build_rope_cache, k_write_kv_cache), src/kernel/rope.cu (rope_kernel),
+// src/kernel/tiled_attention.cu:183-269 (gqa_cached_attention_kernel),
+// src/kernel/rmsnorm.cu (rms_norm_kernel); order of use src/core/engine.cu:262-521.
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "af_common.cuh"
+#include "af_internal.h"
+
+using namespace af;
+
+namespace {
+
+// ---------------------------------------------------------------- embedding
+// x[i] = half(table[token * D + i])  (helpers.cu k_embed_lookup_kernel)
+__global__ void embed_kernel(const float* __restrict__ table, const int* __restrict__ d_token,
+                             __half* __restrict__ x, int D) {
+    const int tok = *d_token;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
+        x[i] = __float2half_rn(table[(size_t)tok * D + i]);
+}
+
+// ------------------------------------------------------- RoPE + KV write
+// Blocks 0..NH-1 rotate q heads, NH..NH+NKV-1 rotate k heads and write k and v
+// to the caches at row *d_pos.  Pair (d, d + HD/2) rotates by the position's
+// angle (rope.cu:9-41).  The reference is built with --use_fast_math, which
+// contracts x*c - y*s into one fused multiply-add; `form` picks the operand
+// order of that contraction.
+__device__ __forceinline__ void rope_pair(float x, float y, float c, float s, int form, float& o0, float& o1) {
+    if (form == 0) {
+        o0 = fmaf(x, c, -(y * s));
+        o1 = fmaf(x, s, y * c);
+    } else {
+        o0 = fmaf(-y, s, x * c);
+        o1 = fmaf(y, c, x * s);
+    }
+}
+
+__global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict__ cos_tab,
+                               const float* __restrict__ sin_tab, const int* __restrict__ d_pos,
+                               __half* __restrict__ k_cache, __half* __restrict__ v_cache, int NH, int NKV, int HD,
+                               int form) {
+    const int pos = *d_pos;
+    const int h = blockIdx.x, half_hd = HD / 2;
+    const int q_dim = NH * HD, kv_dim = NKV * HD;
+    for (int d = threadIdx.x; d < half_hd; d += blockDim.x) {
+        const float c = cos_tab[(size_t)pos * half_hd + d], s = sin_tab[(size_t)pos * half_hd + d];
+        __half* base = h < NH ? qkv + (size_t)h * HD : qkv + q_dim + (size_t)(h - NH) * HD;
+        float o0, o1;
+        rope_pair(__half2float(base[d]), __half2float(base[d + half_hd]), c, s, form, o0, o1);
+        const __half r0 = __float2half_rn(o0), r1 = __float2half_rn(o1);
+        base[d] = r0;
+        base[d + half_hd] = r1;
+        if (h >= NH) {   // write_kv_cache (helpers.cu k_write_kv_cache): rotated k and v
+            const size_t row = (size_t)pos * kv_dim + (size_t)(h - NH) * HD;
+            k_cache[row + d] = r0;
+            k_cache[row + d + half_hd] = r1;
+            const __half* v = qkv + q_dim + kv_dim + (size_t)(h - NH) * HD;
+            v_cache[row + d] = v[d];
+            v_cache[row + d + half_hd] = v[d + half_hd];
+        }
+    }
+}
+
+// ------------------------------------------------------ cached attention
+// Split-KV GQA attention for one token.  CTA (split, kv head) handles
+// positions [t0, t1) of the cache for the G = NH/NKV query heads that share
+// the kv head; each of its 4 warps takes every 4th position with an online
+// softmax (lane l holds dims 4l..4l+3).  The CTA's partial (max, sum, o) goes
+// to the workspace; the last CTA of the kv head merges the splits in split
+// order (deterministic) and writes out, then re-zeroes its counter.
+constexpr int kAttnSplits = 32;
+constexpr int kAttnMaxG = 8;
+constexpr int kAttnWarps = 4;
+
+__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
+    const int* __restrict__ d_pos, __half* __restrict__ out, int NH, int NKV, float* __restrict__ part,
+    int* __restrict__ counters) {
+    constexpr int HD = 128;
+    const int split = blockIdx.x, kvh = blockIdx.y, G = NH / NKV;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int seq = *d_pos + 1;
+    const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
+    const int t0 = min(seq, split * chunk), t1 = min(seq, t0 + chunk);
+    const int kv_dim = NKV * HD;
+    const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
+
+    float qv[kAttnMaxG][4];
+    for (int g = 0; g < G; ++g) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(q + (size_t)(kvh * G + g) * HD + lane * 4);
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        qv[g][0] = __low2float(a);
+        qv[g][1] = __high2float(a);
+        qv[g][2] = __low2float(b);
+        qv[g][3] = __high2float(b);
+    }
+    float m[kAttnMaxG], l[kAttnMaxG], o[kAttnMaxG][4];
+    for (int g = 0; g < kAttnMaxG; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+        o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    }
+    for (int t = t0 + warp; t < t1; t += kAttnWarps) {
+        const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
+        const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
+        const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
+        const __half2 k0 = *reinterpret_cast<const __half2*>(&kr.x), k1 = *reinterpret_cast<const __half2*>(&kr.y);
+        const __half2 v0 = *reinterpret_cast<const __half2*>(&vr.x), v1 = *reinterpret_cast<const __half2*>(&vr.y);
+        const float kf[4] = {__low2float(k0), __high2float(k0), __low2float(k1), __high2float(k1)};
+        const float vf[4] = {__low2float(v0), __high2float(v0), __low2float(v1), __high2float(v1)};
+        for (int g = 0; g < G; ++g) {
+            float sdot = qv[g][0] * kf[0];
+            sdot = fmaf(qv[g][1], kf[1], sdot);
+            sdot = fmaf(qv[g][2], kf[2], sdot);
+            sdot = fmaf(qv[g][3], kf[3], sdot);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+            const float sc = sdot * scale;
+            const float mn = fmaxf(m[g], sc);
+            const float corr = __expf(m[g] - mn);   // 0 on the first position (m = -inf)
+            const float pw = __expf(sc - mn);
+            l[g] = l[g] * corr + pw;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
+            m[g] = mn;
+        }
+    }
+    // merge the 4 warps through shared memory, then this CTA's partial to the workspace
+    __shared__ float s_m[kAttnWarps][kAttnMaxG], s_l[kAttnWarps][kAttnMaxG];
+    __shared__ float s_o[kAttnWarps][kAttnMaxG][HD];
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            s_m[warp][g] = m[g];
+            s_l[warp][g] = l[g];
+        }
+        for (int e = 0; e < 4; ++e) s_o[warp][g][lane * 4 + e] = o[g][e];
+    }
+    __syncthreads();
+    const int rec = 2 + HD;   // (m, l, o[HD]) per query head
+    float* my = part + ((size_t)kvh * kAttnSplits + split) * G * rec;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int g = i / HD, d = i % HD;
+        float mm = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
+        float ll = 0.f, oo = 0.f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
+            ll = fmaf(s_l[w][g], f, ll);
+            oo = fmaf(s_o[w][g][d], f, oo);
+        }
+        __stcg(my + g * rec + 2 + d, oo);
+        if (d == 0) {
+            __stcg(my + g * rec, mm);
+            __stcg(my + g * rec + 1, ll);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(counters + kvh, 1) == kAttnSplits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* all = part + (size_t)kvh * kAttnSplits * G * rec;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int g = i / HD, d = i % HD;
+        float mm = -INFINITY;
+        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ldcg_f32(all + (size_t)sp * G * rec + g * rec));
+        float ll = 0.f, oo = 0.f;
+        for (int sp = 0; sp < kAttnSplits; ++sp) {
+            const float* r = all + (size_t)sp * G * rec + g * rec;
+            const float ms = ldcg_f32(r);
+            if (ms == -INFINITY) continue;   // an empty split
+            const float f = __expf(ms - mm);
+            ll = fmaf(ldcg_f32(r + 1), f, ll);
+            oo = fmaf(ldcg_f32(r + 2 + d), f, oo);
+        }
+        out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0;   // leave the workspace counter at zero
+}
+
+// ------------------------------------------------------------- RMSNorm
+// The reference's rms_norm_kernel<half, 128> arithmetic (rmsnorm.cu:9-67):
+// 128 threads, strided FMA sums, each warp's shuffle-down tree, the four warp
+// sums in order, rsqrt(sum / K + eps) with the fast-math instructions, and
+// half(x * r * w).
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const __half* __restrict__ x, const float* __restrict__ w,
+                                                      float eps, __half* __restrict__ out, int K) {
+    __shared__ float s_nrm[4];
+    __shared__ float s_r;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K; i += 128) {
+        const float v = __half2float(x[i]);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) ss += __shfl_down_sync(0xffffffffu, ss, o);
+    if (lane == 0) s_nrm[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0)
+        s_r = rsqrt_approx_ftz(fdiv_full_ftz(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], (float)K) + eps);
+    __syncthreads();
+    const float r = s_r;
+    for (int i = threadIdx.x; i < K; i += 128) out[i] = __float2half_rn(__half2float(x[i]) * r * w[i]);
+}
+
+__global__ void advance_kernel(int* d_pos, int by) { *d_pos += by; }
+
+int g_rope_form = 0;   // operand order of the RoPE contraction (see rope_pair)
+
+}  // namespace
+
+extern "C" af_status af_embed_lookup(const float* table, const int* d_token, void* x, int D, void* stream) {
+    if (table == nullptr || d_token == nullptr || x == nullptr || D <= 0 || !aligned(x, 2)) return AF_ERR_INVALID;
+    embed_kernel<<<(D + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        table, d_token, static_cast<__half*>(x), D);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "embed_kernel");
+}
+
+extern "C" af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq, int head_dim, float base) {
+    if (cos_out == nullptr || sin_out == nullptr || max_seq <= 0 || head_dim <= 0 || head_dim % 2) return AF_ERR_INVALID;
+    // the reference's host formula (helpers.cu build_rope_cache), in float
+    const int half_dim = head_dim / 2;
+    for (int s = 0; s < max_seq; ++s)
+        for (int i = 0; i < half_dim; ++i) {
+            const float theta = s / std::pow(base, 2.0f * i / head_dim);
+            cos_out[(size_t)s * half_dim + i] = std::cos(theta);
+            sin_out[(size_t)s * half_dim + i] = std::sin(theta);
+        }
+    return AF_OK;
+}
+
+extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
+                                     void* k_cache, void* v_cache, int n_heads, int n_kv_heads, int head_dim,
+                                     void* stream) {
+    if (qkv == nullptr || cos_tab == nullptr || sin_tab == nullptr || d_pos == nullptr || k_cache == nullptr ||
+        v_cache == nullptr || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2)
+        return AF_ERR_INVALID;
+    rope_kv_kernel<<<n_heads + n_kv_heads, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<__half*>(qkv), cos_tab, sin_tab, d_pos, static_cast<__half*>(k_cache),
+        static_cast<__half*>(v_cache), n_heads, n_kv_heads, head_dim, g_rope_form);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "rope_kv_kernel");
+}
+
+extern "C" af_status af_rope_set_form(int form) {
+    if (form != 0 && form != 1) return AF_ERR_INVALID;
+    g_rope_form = form;
+    return AF_OK;
+}
+
+extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads) {
+    if (n_kv_heads <= 0 || n_heads % n_kv_heads) return 0;
+    const size_t g = n_heads / n_kv_heads;
+    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_kv_heads * kAttnSplits * g * (2 + 128) * 4;
+}
+
+extern "C" af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
+                                        void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+    if (q == nullptr || k_cache == nullptr || v_cache == nullptr || d_pos == nullptr || out == nullptr ||
+        n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+        return AF_ERR_INVALID;
+    if (head_dim != 128 || n_heads / n_kv_heads > kAttnMaxG) return AF_ERR_UNSUPPORTED;
+    if (!aligned(q, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) || !aligned(out, 2)) return AF_ERR_INVALID;
+    const size_t need = af_decode_attention_workspace_bytes(n_heads, n_kv_heads);
+    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) return AF_ERR_WORKSPACE;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    int* counters = reinterpret_cast<int*>(ws + 256);
+    float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
+    attention_kernel<<<dim3(kAttnSplits, n_kv_heads), kAttnWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(q), static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
+        d_pos, static_cast<__half*>(out), n_heads, n_kv_heads, part, counters);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_kernel");
+}
+
+extern "C" af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream) {
+    if (x == nullptr || norm_w == nullptr || out == nullptr || K <= 0 || !aligned(x, 2) || !aligned(out, 2))
+        return AF_ERR_INVALID;
+    rmsnorm_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(x), norm_w, eps,
+                                                                    static_cast<__half*>(out), K);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "rmsnorm_kernel");
+}
+
+extern "C" af_status af_decode_advance(int* d_pos, int by, void* stream) {
+    if (d_pos == nullptr) return AF_ERR_INVALID;
+    advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(d_pos, by);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "advance_kernel");
+}

@@ -97,28 +97,31 @@ def _header(shape: ModelShape) -> bytes:
     return h + b"\0" * (ALIGN - len(h))
 
 
-def _rng(seed: int, tag: str) -> torch.Generator:
-    g = torch.Generator()
+def _rng(seed: int, tag: str, device="cpu") -> torch.Generator:
+    g = torch.Generator(device=device)
     g.manual_seed((seed * 1_000_003 + sum((i + 1) * ord(ch) for i, ch in enumerate(tag))) % (2**63))
     return g
 
 
-def tensor_values(shape: ModelShape, name: str, seed: int = 0):
+def tensor_values(shape: ModelShape, name: str, seed: int = 0, device="cpu"):
     """The values written for block `name` (numpy, in the stored dtype); a
-    linear weight and its scales come together from `name` = layers.i.proj."""
-    g = _rng(seed, name)
+    linear weight and its scales come together from `name` = layers.i.proj.
+    The draw depends on the generating device (device="cuda" is much faster
+    for full-size files); a given (seed, device) always gives the same file."""
+    g = _rng(seed, name, device)
+    kw = dict(generator=g, device=device)
     if name in ("embed", "lm_head"):
-        v = (torch.randn(shape.vocab, shape.dim, generator=g) * 0.02).half()
+        v = (torch.randn(shape.vocab, shape.dim, **kw) * 0.02).half().cpu()
         return v.float().numpy() if name == "embed" else v.view(torch.int16).numpy().view(np.uint16)
     if name.endswith("norm"):
-        return (1.0 + 0.1 * torch.randn(shape.dim, generator=g)).half().float().numpy()
+        return (1.0 + 0.1 * torch.randn(shape.dim, **kw)).half().float().cpu().numpy()
     proj = name.split(".")[-1]
     n, k = {nm: (n, k) for nm, n, k in shape.linears()}[proj]
-    q, s = quantize_gs128(torch.randn(n, k, generator=g) * 0.02)
-    return q.view(torch.uint8).numpy(), s.view(torch.int16).numpy().view(np.uint16)
+    q, s = quantize_gs128(torch.randn(n, k, **kw) * 0.02)
+    return q.view(torch.uint8).cpu().numpy(), s.view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def write_synthetic_bin(path, shape: ModelShape = ModelShape(), seed: int = 0) -> int:
+def write_synthetic_bin(path, shape: ModelShape = ModelShape(), seed: int = 0, device="cpu") -> int:
     """Write a random-init model file; returns its size in bytes."""
     plan, total = block_plan(shape)
     path = Path(path)
@@ -128,7 +131,7 @@ def write_synthetic_bin(path, shape: ModelShape = ModelShape(), seed: int = 0) -
             if name.endswith("_scales"):
                 continue   # written together with its weights
             assert f.tell() == off, (name, f.tell(), off)
-            v = tensor_values(shape, name, seed)
+            v = tensor_values(shape, name, seed, device)
             blobs = v if isinstance(v, tuple) else (v,)
             for b in blobs:
                 raw = np.ascontiguousarray(b).tobytes()

@@ -174,6 +174,39 @@ af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const v
                                            int K, int group_size, af_scale_kind kind, af_tp_comm* comm,
                                            void* stream);
 
+/* ------------------------------------------------- rest of a decode step ---
+ * With these and the projections above, a whole greedy decode step (embedding
+ * .. argmax) runs on device-side state -- the token id and the position live
+ * in device ints -- so consecutive steps replay one captured CUDA graph.
+ * Layouts are the reference engine's: qkv FP16 [NH*HD | NKV*HD | NKV*HD]
+ * (engine.cu:315), caches FP16 [max_seq, NKV*HD] per layer (engine.cu:196-209),
+ * RoPE tables FP32 [max_seq, HD/2].
+ *   af_embed_lookup      x = half(table[*d_token])      (helpers.cu k_embed_lookup_kernel)
+ *   af_rope_tables       host: cos/sin tables, the reference's float formula
+ *                        (helpers.cu build_rope_cache), base 500000 for Llama 3
+ *   af_rope_kv_write     rotate q and k in qkv at *d_pos, write k and v to row
+ *                        *d_pos of the caches (rope.cu; helpers.cu k_write_kv_cache)
+ *   af_decode_attention  softmax(q k^T / sqrt(HD)) v over positions 0..*d_pos,
+ *                        GQA (NH % NKV == 0, NH/NKV <= 8), HD = 128; split over
+ *                        the cache, deterministic merge.  Workspace: zeroed once
+ *                        (af_workspace_reset), one per stream; every call leaves
+ *                        it zeroed.  (tiled_attention.cu gqa_cached_attention_kernel)
+ *   af_rmsnorm           the reference's rms_norm arithmetic, one vector
+ *   af_decode_advance    *d_pos += by (the step's last launch)
+ * af_rope_set_form picks the operand order of RoPE's fused multiply-add (0 or
+ * 1), kept for the parity test that pins it against the reference kernel. */
+af_status af_embed_lookup(const float* table, const int* d_token, void* x, int D, void* stream);
+af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq, int head_dim, float base);
+af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos, void* k_cache,
+                           void* v_cache, int n_heads, int n_kv_heads, int head_dim, void* stream);
+af_status af_rope_set_form(int form);
+size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads);
+af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos, void* out,
+                              int n_heads, int n_kv_heads, int head_dim, void* workspace, size_t workspace_bytes,
+                              void* stream);
+af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream);
+af_status af_decode_advance(int* d_pos, int by, void* stream);
+
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for
  * callers that cannot allocate device memory (no cudaMalloc available or

@@ -57,6 +57,30 @@ def cpu():
     return _cpu
 
 
+_ref_engine = None
+
+
+def ref_engine():
+    """The reference's decode engine (GPU), or None if _ref/libafref_engine.so is absent."""
+    global _ref_engine
+    if _ref_engine is None:
+        path = HERE / "_ref" / "libafref_engine.so"
+        if not path.exists():
+            return None
+        L = ctypes.CDLL(str(path))
+        vp, i = ctypes.c_void_p, ctypes.c_int
+        L.afref_engine_create.restype = vp
+        L.afref_engine_create.argtypes = [ctypes.c_char_p]
+        L.afref_engine_destroy.restype = None
+        L.afref_engine_destroy.argtypes = [vp]
+        L.afref_engine_step.restype = i
+        L.afref_engine_step.argtypes = [vp, i, i]
+        L.afref_engine_tpot_ms.restype = ctypes.c_float
+        L.afref_engine_tpot_ms.argtypes = [vp, i, i, i]
+        _ref_engine = L
+    return _ref_engine
+
+
 def ref():
     """The reference's kernels (GPU), or None if _ref/libafref.so is absent."""
     global _ref
@@ -78,6 +102,12 @@ def ref():
         L.afref_swiglu.argtypes = [vp, vp, vp, i, vp]
         L.afref_residual_add.restype = i
         L.afref_residual_add.argtypes = [vp, vp, i, vp]
+        L.afref_rope_kv.restype = i
+        L.afref_rope_kv.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
+        L.afref_rope_cache.restype = i
+        L.afref_rope_cache.argtypes = [vp, vp, i, i, ctypes.c_float, vp]
+        L.afref_cached_attention.restype = i
+        L.afref_cached_attention.argtypes = [vp, vp, vp, vp, i, i, i, i, vp]
         _ref = L
     return _ref
 

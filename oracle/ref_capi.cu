@@ -70,3 +70,33 @@ extern "C" int afref_residual_add(void* inout, const void* sub, int N, void* str
     launch_residual_add(iv, sv, static_cast<cudaStream_t>(stream));
     return (int)cudaGetLastError();
 }
+
+// RoPE on one token at a position (engine.cu:334-346: cos/sin pointers offset by the position, seq 1),
+// then the KV-cache write (engine.cu:350-355).
+extern "C" int afref_rope_kv(void* qkv, const float* d_cos, const float* d_sin, void* k_cache, void* v_cache,
+                             int pos, int NH, int NKV, int HD, void* stream) {
+    const int q_dim = NH * HD, kv_dim = NKV * HD;
+    half* base = static_cast<half*>(qkv);
+    View qv = create_contiguous_view(base, DataType::FP16, {1, q_dim});
+    View kv = create_contiguous_view(base + q_dim, DataType::FP16, {1, kv_dim});
+    launch_rope(qv, kv, d_cos + (size_t)pos * (HD / 2), d_sin + (size_t)pos * (HD / 2), 1, NKV, NH, HD,
+                static_cast<cudaStream_t>(stream));
+    View all = create_contiguous_view(qkv, DataType::FP16, {1, q_dim + 2 * kv_dim});
+    View kc = create_contiguous_view(k_cache, DataType::FP16, {2048, kv_dim});
+    View vc = create_contiguous_view(v_cache, DataType::FP16, {2048, kv_dim});
+    launch_write_kv_cache(all, kc, vc, pos, q_dim, kv_dim, static_cast<cudaStream_t>(stream));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int afref_rope_cache(float* d_cos, float* d_sin, int max_seq, int HD, float base, void* stream) {
+    build_rope_cache(d_cos, d_sin, max_seq, HD, base, static_cast<cudaStream_t>(stream));
+    return (int)cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int afref_cached_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                      int seq_len, int HD, int NH, int NKV, void* stream) {
+    launch_cached_attention(static_cast<const half*>(q), static_cast<const half*>(k_cache),
+                            static_cast<const half*>(v_cache), static_cast<half*>(out), seq_len, HD, NH, NKV,
+                            static_cast<cudaStream_t>(stream));
+    return (int)cudaGetLastError();
+}

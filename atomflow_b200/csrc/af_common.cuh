@@ -157,10 +157,23 @@ __device__ __forceinline__ float fdiv_full_ftz(float a, float b) {
     asm("div.full.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
     return r;
 }
+__device__ __forceinline__ float rcp_approx_ftz(float a) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
+}
 __device__ __forceinline__ float rsqrt_approx_ftz(float a) {
     float r;
     asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
     return r;
+}
+// The reference's RMSNorm scale (rmsnorm.cu:47), as its fast-math build
+// evaluates it: the division by K becomes a multiply by the approximate
+// reciprocal, contracted with the + eps, then the approximate rsqrt.
+// (Checked bit for bit against the reference kernel on 1500 random vectors;
+// a true or approximate division differs on about 1 in 80.)
+__device__ __forceinline__ float rms_scale_ref(float sum_sq, int K, float eps) {
+    return rsqrt_approx_ftz(fmaf(sum_sq, rcp_approx_ftz((float)K), eps));
 }
 
 // 64-bit single-copy-atomic accesses visible across GPUs (peer memory over NVLink)

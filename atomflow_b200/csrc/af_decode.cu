@@ -74,19 +74,23 @@ __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict
 // Split-KV GQA attention for one token.  CTA (split, kv head) handles
 // positions [t0, t1) of the cache for the G = NH/NKV query heads that share
 // the kv head; each of its 4 warps takes every 4th position with an online
-// softmax (lane l holds dims 4l..4l+3).  The CTA's partial (max, sum, o) goes
-// to the workspace; the last CTA of the kv head merges the splits in split
-// order (deterministic) and writes out, then re-zeroes its counter.
+// softmax (lane l holds dims 4l..4l+3; two positions' loads in flight).  The
+// CTA's partial (max, sum, o) goes to the workspace; the last CTA of the kv
+// head merges the splits in split order (deterministic) and writes out, then
+// re-zeroes its counter.  (A lane-per-position layout -- one k row per lane,
+// then p.v by dims -- was measured slower at 1-2k positions: with 32 splits
+// a CTA has ~32 positions, which left one warp doing all of them.)
 constexpr int kAttnSplits = 32;
 constexpr int kAttnMaxG = 8;
 constexpr int kAttnWarps = 4;
 
+template <int G>
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
-    const int* __restrict__ d_pos, __half* __restrict__ out, int NH, int NKV, float* __restrict__ part,
+    const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
     int* __restrict__ counters) {
     constexpr int HD = 128;
-    const int split = blockIdx.x, kvh = blockIdx.y, G = NH / NKV;
+    const int split = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int seq = *d_pos + 1;
     const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
@@ -94,7 +98,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const int kv_dim = NKV * HD;
     const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
 
-    float qv[kAttnMaxG][4];
+    float qv[G][4];
+#pragma unroll
     for (int g = 0; g < G; ++g) {
         const uint2 raw = *reinterpret_cast<const uint2*>(q + (size_t)(kvh * G + g) * HD + lane * 4);
         const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
@@ -103,20 +108,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
         qv[g][2] = __low2float(b);
         qv[g][3] = __high2float(b);
     }
-    float m[kAttnMaxG], l[kAttnMaxG], o[kAttnMaxG][4];
-    for (int g = 0; g < kAttnMaxG; ++g) {
+    float m[G], l[G], o[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
         o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
     }
-    for (int t = t0 + warp; t < t1; t += kAttnWarps) {
+    auto load = [&](int t, float (&kf)[4], float (&vf)[4]) {
         const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
         const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
         const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
         const __half2 k0 = *reinterpret_cast<const __half2*>(&kr.x), k1 = *reinterpret_cast<const __half2*>(&kr.y);
         const __half2 v0 = *reinterpret_cast<const __half2*>(&vr.x), v1 = *reinterpret_cast<const __half2*>(&vr.y);
-        const float kf[4] = {__low2float(k0), __high2float(k0), __low2float(k1), __high2float(k1)};
-        const float vf[4] = {__low2float(v0), __high2float(v0), __low2float(v1), __high2float(v1)};
+        kf[0] = __low2float(k0);
+        kf[1] = __high2float(k0);
+        kf[2] = __low2float(k1);
+        kf[3] = __high2float(k1);
+        vf[0] = __low2float(v0);
+        vf[1] = __high2float(v0);
+        vf[2] = __low2float(v1);
+        vf[3] = __high2float(v1);
+    };
+    auto consume = [&](const float (&kf)[4], const float (&vf)[4]) {
+#pragma unroll
         for (int g = 0; g < G; ++g) {
             float sdot = qv[g][0] * kf[0];
             sdot = fmaf(qv[g][1], kf[1], sdot);
@@ -133,25 +148,42 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
             for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
             m[g] = mn;
         }
+    };
+    int t = t0 + warp;
+    for (; t + kAttnWarps < t1; t += 2 * kAttnWarps) {
+        float ka[4], va[4], kb[4], vb[4];
+        load(t, ka, va);
+        load(t + kAttnWarps, kb, vb);
+        consume(ka, va);
+        consume(kb, vb);
+    }
+    if (t < t1) {
+        float ka[4], va[4];
+        load(t, ka, va);
+        consume(ka, va);
     }
     // merge the 4 warps through shared memory, then this CTA's partial to the workspace
-    __shared__ float s_m[kAttnWarps][kAttnMaxG], s_l[kAttnWarps][kAttnMaxG];
-    __shared__ float s_o[kAttnWarps][kAttnMaxG][HD];
+    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+    __shared__ float s_o[kAttnWarps][G][HD];
+#pragma unroll
     for (int g = 0; g < G; ++g) {
         if (lane == 0) {
             s_m[warp][g] = m[g];
             s_l[warp][g] = l[g];
         }
+#pragma unroll
         for (int e = 0; e < 4; ++e) s_o[warp][g][lane * 4 + e] = o[g][e];
     }
     __syncthreads();
-    const int rec = 2 + HD;   // (m, l, o[HD]) per query head
+    constexpr int rec = 2 + HD;   // (m, l, o[HD]) per query head
     float* my = part + ((size_t)kvh * kAttnSplits + split) * G * rec;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float mm = -INFINITY;
+#pragma unroll
         for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
         float ll = 0.f, oo = 0.f;
+#pragma unroll
         for (int w = 0; w < kAttnWarps; ++w) {
             const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
             ll = fmaf(s_l[w][g], f, ll);
@@ -173,16 +205,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const float* all = part + (size_t)kvh * kAttnSplits * G * rec;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
-        float mm = -INFINITY;
-        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ldcg_f32(all + (size_t)sp * G * rec + g * rec));
-        float ll = 0.f, oo = 0.f;
-        for (int sp = 0; sp < kAttnSplits; ++sp) {
+        float ms[kAttnSplits], ls[kAttnSplits], os[kAttnSplits];
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) {   // independent loads, all in flight
             const float* r = all + (size_t)sp * G * rec + g * rec;
-            const float ms = ldcg_f32(r);
-            if (ms == -INFINITY) continue;   // an empty split
-            const float f = __expf(ms - mm);
-            ll = fmaf(ldcg_f32(r + 1), f, ll);
-            oo = fmaf(ldcg_f32(r + 2 + d), f, oo);
+            ms[sp] = ldcg_f32(r);
+            ls[sp] = ldcg_f32(r + 1);
+            os[sp] = ldcg_f32(r + 2 + d);
+        }
+        float mm = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ms[sp]);
+        float ll = 0.f, oo = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) {   // split order: deterministic
+            const float f = ms[sp] == -INFINITY ? 0.f : __expf(ms[sp] - mm);   // empty splits add nothing
+            ll = fmaf(ls[sp], f, ll);
+            oo = fmaf(os[sp], f, oo);
         }
         out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
     }
@@ -192,7 +231,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
 // ------------------------------------------------------------- RMSNorm
 // The reference's rms_norm_kernel<half, 128> arithmetic (rmsnorm.cu:9-67):
 // 128 threads, strided FMA sums, each warp's shuffle-down tree, the four warp
-// sums in order, rsqrt(sum / K + eps) with the fast-math instructions, and
+// sums in order, the reference build's rsqrt(sum / K + eps) (rms_scale_ref), and
 // half(x * r * w).
 __global__ void __launch_bounds__(128) rmsnorm_kernel(const __half* __restrict__ x, const float* __restrict__ w,
                                                       float eps, __half* __restrict__ out, int K) {
@@ -209,7 +248,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const __half* __restrict__
     if (lane == 0) s_nrm[warp] = ss;
     __syncthreads();
     if (threadIdx.x == 0)
-        s_r = rsqrt_approx_ftz(fdiv_full_ftz(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], (float)K) + eps);
+        s_r = rms_scale_ref(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], K, eps);
     __syncthreads();
     const float r = s_r;
     for (int i = threadIdx.x; i < K; i += 128) out[i] = __float2half_rn(__half2float(x[i]) * r * w[i]);
@@ -280,9 +319,17 @@ extern "C" af_status af_decode_attention(const void* q, const void* k_cache, con
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     int* counters = reinterpret_cast<int*>(ws + 256);
     float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
-    attention_kernel<<<dim3(kAttnSplits, n_kv_heads), kAttnWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(q), static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
-        d_pos, static_cast<__half*>(out), n_heads, n_kv_heads, part, counters);
+    const dim3 grid(kAttnSplits, n_kv_heads), block(kAttnWarps * 32);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
+                 *vh = static_cast<const __half*>(v_cache);
+    __half* oh = static_cast<__half*>(out);
+    switch (n_heads / n_kv_heads) {
+#define AF_ATTN(GG) \
+    case GG: attention_kernel<GG><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters); break;
+        AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
+#undef AF_ATTN
+    }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_kernel");
 }

@@ -664,8 +664,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         }
         __syncthreads();
         if (threadIdx.x == 0)
-            s_rms = rsqrt_approx_ftz(fdiv_full_ftz(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], (float)p.K) +
-                                     p.norm_eps);
+            s_rms = rms_scale_ref(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], p.K, p.norm_eps);
         __syncthreads();
         const float r = s_rms;
         for (int i = threadIdx.x; i < p.K; i += kThreads) xs[i] = __float2half_rn(__half2float(xs[i]) * r * gam[i]);

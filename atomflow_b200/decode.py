@@ -126,6 +126,13 @@ class DecodeEngine:
             self._launch_step(self.stream.cuda_stream, advance=advance)
         return g
 
+    def replay(self, g: torch.cuda.CUDAGraph):
+        """Replay a captured step on the engine's stream (CUDAGraph.replay
+        alone would launch on torch's current stream, unordered with the
+        engine's token and position writes)."""
+        with torch.cuda.stream(self.stream):
+            g.replay()
+
     launches_per_step = None   # set on the first step
 
     # ---- one step

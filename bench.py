@@ -484,6 +484,131 @@ def cpu_baseline(items, budget_s=10.0):
 
 # -------------------------------------------------------------------- main
 
+DECODE_POS = 1024
+
+
+def decode_model_path():
+    """BASELINE config 3's random-init model in the reference's .bin format,
+    written once per box (generated on the GPU) and shared by both arms."""
+    from atomflow_b200.weights_bin import ModelShape, write_synthetic_bin
+    path = Path(os.environ.get("AF_DECODE_BIN", "/tmp/af_decode_llama3.2-3b_seed0.bin"))
+    if not path.exists():
+        tmp = path.with_suffix(".part")
+        write_synthetic_bin(tmp, ModelShape(), seed=0, device="cuda")
+        tmp.rename(path)
+    return path
+
+
+def run_decode(args, device, local):
+    """Greedy decode of a Llama-3.2-3B-shaped model (config 3): KV cache
+    prefilled to 1024 positions by teacher-forced steps with seeded random
+    tokens, then `steps` greedy steps.  Ours: DecodeEngine, one CUDA-graph
+    replay per token, position and token kept on the device.  Reference: its
+    own AtomFlowEngine (oracle/_ref), TPOT as its main.cu measures it -- one
+    graph of forward_pass at position 1024, replayed."""
+    path = decode_model_path()
+    sampler = ClockSampler(local)
+    sampler.wait_first()
+    peak, peak_kind = measured_peaks()
+    config = {"workload": "llama3.2-3b-shaped greedy decode, 28 layers, random-init weights in the reference .bin "
+                          "format (BASELINE config 3)", "position": DECODE_POS, "M": 1,
+              "kv_cache": f"prefilled to {DECODE_POS} positions by teacher-forced steps (seeded random tokens)",
+              "l2": "5.2 GB of weights per step >> 126 MB L2 (no flush needed)", "parallelism": "single"}
+    out = {"metric": "decode tok/s (Llama-3.2-3B-shaped, M=1, KV cache at 1024 positions)", "unit": "tok/s",
+           "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "fp8e4m3 weights x fp16 act, fp32 accum", "data": "synthetic seeded",
+           "config": config}
+    if args.impl == "reference":
+        import oracle
+        R = oracle.ref_engine()
+        if R is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libafref_engine.so not built"}))
+            return 0
+        h = R.afref_engine_create(str(path).encode())
+        t0 = time.time()
+        ms = float(R.afref_engine_tpot_ms(h, DECODE_POS, args.steps, args.warmup))
+        t1 = time.time()
+        sampler.stop()
+        if ms <= 0:
+            raise RuntimeError(f"reference TPOT measurement failed ({ms})")
+        out.update({"impl": "reference", "value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 5),
+                    "clocks": sampler.summary(t0, t1), "gpu_launches": 0,
+                    "e2e": {"value": round(1000.0 / ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0},
+                    "cpu_baseline": {"value": round(1000.0 / ms, 2), "unit": "tok/s", "cores": None,
+                                     "kind": "reference", "sample": "the reference's AtomFlowEngine (CUDA, compiled "
+                                     "from its sources), graph of forward_pass at position 1024, on this GPU"}})
+        print(json.dumps(out))
+        os._exit(0)
+    from atomflow_b200.decode import DecodeEngine
+    eng = DecodeEngine(path)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, 65536, DECODE_POS).tolist()
+    g = eng.capture(advance=True)
+    eng.current_pos = 0
+    if os.environ.get("AF_DECODE_PREFILL", "1") != "0":   # "0": profiling runs only (the cache's
+        for t in prompt:                                  # contents change no kernel's work)
+            eng.inject_token(t)
+            eng.replay(g)
+    else:
+        config["kv_cache"] = "not prefilled (profiling run)"
+        eng.current_pos = DECODE_POS
+    eng.stream.synchronize()
+    assert eng.current_pos == DECODE_POS
+    for _ in range(args.warmup):          # greedy warm-up steps, then rewind
+        eng.replay(g)
+    eng.current_pos = DECODE_POS
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eng.stream.synchronize()
+    t0 = time.time()
+    ev0.record(eng.stream)
+    for _ in range(args.steps):
+        eng.replay(g)
+    ev1.record(eng.stream)
+    eng.stream.synchronize()
+    t1 = time.time()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clocks = sampler.summary(t0, t1)
+    # end to end: each step the host sends the token and reads the next one (pinned, inside the graph)
+    tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+    tok_back = torch.zeros(1, dtype=torch.int32).pin_memory()
+    ge = torch.cuda.CUDAGraph()
+    eng.current_pos = DECODE_POS
+    eng.stream.synchronize()
+    with torch.cuda.graph(ge, stream=eng.stream):
+        eng.d_token.copy_(tok_h, non_blocking=True)
+        eng._launch_step(eng.stream.cuda_stream, advance=True)
+        tok_back.copy_(eng.d_token, non_blocking=True)
+    eng.current_pos = DECODE_POS
+    for _ in range(3):
+        eng.replay(ge)
+    eng.current_pos = DECODE_POS
+    eng.stream.synchronize()
+    ev0.record(eng.stream)
+    for _ in range(args.steps):
+        eng.replay(ge)
+    ev1.record(eng.stream)
+    eng.stream.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    sampler.stop()
+    step_bytes = eng.weight_bytes() + eng.kv_bytes(DECODE_POS + args.steps // 2)
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    out.update({"value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 5), "clocks": clocks,
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 4),
+                             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                             "traffic": None, "kernel": "whole step (GEMV kernels carry 94% of the bytes)",
+                             "per_launch": f"{step_bytes / 1e9:.3f} GB per step (weights, scales, norms, lm_head, "
+                                           f"embedding row, KV cache) over {ms * 1e3:.1f} us"},
+                "gpu_launches": eng.launches_per_step * args.steps,
+                "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 5),
+                        "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                        "path": "DecodeEngine over the C ABI: token H2D from pinned memory, the step, next token D2H "
+                                "to pinned memory, one CUDA graph per step"}})
+    print(json.dumps(out))
+    os._exit(0)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,6 +639,10 @@ def main():
     trank = rank if tp > 1 else 0
 
     wl = args.workload
+    if wl == "decode":
+        if world > 1:
+            raise SystemExit("the decode workload runs on one GPU")
+        return run_decode(args, device, local)
     if wl == "layerset":
         items = make_layerset(device, trank, tp, layers=args.layers)
         config = {"workload": f"llama3.2-3b layer-set x{args.layers} (BASELINE config 1)", "M": 1,

@@ -99,9 +99,13 @@ def test_embed_and_rmsnorm_match_reference():
     assert L.af_embed_lookup(table.data_ptr(), tok.data_ptr(), x.data_ptr(), D, st()) == 0
     torch.cuda.synchronize()
     assert torch.equal(x, table[777].half())
-    for K, scale in ((3072, 1.0), (1024, 40.0), (200, 0.01)):
-        xx = (torch.randn(K, device="cuda") * scale).half()
-        w = (1 + 0.1 * torch.randn(K, device="cuda")).float()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(123)
+    # many vectors: a wrong rounding form of the norm shows on about 1 vector in 80
+    for it in range(300):
+        K, scale = ((3072, 1.0), (1024, 40.0), (200, 0.01), (4096, 3.0))[it % 4]
+        xx = (torch.randn(K, generator=gen, device="cuda") * scale).half()
+        w = (1 + 0.1 * torch.randn(K, generator=gen, device="cuda")).float()
         a = torch.zeros(K, dtype=torch.float16, device="cuda")
         b = torch.zeros_like(a)
         assert L.af_rmsnorm(xx.data_ptr(), w.data_ptr(), 1e-5, a.data_ptr(), K, st()) == 0
@@ -191,7 +195,7 @@ def test_decode_engine_tokens_match_reference(tmp_path):
         ours.current_pos = 16
         ours.inject_token(seq_a[0])
         for i in range(8):
-            g.replay()
+            ours.replay(g)
             assert ours.get_output_token() == seq_a[i + 1]
     finally:
         R.afref_engine_destroy(theirs)

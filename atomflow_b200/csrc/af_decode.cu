@@ -10,6 +10,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdint>
 
 #include "af_common.cuh"
@@ -73,7 +74,7 @@ __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict
 // ------------------------------------------------------ cached attention
 // Split-KV GQA attention for one token.  CTA (split, kv head) handles
 // positions [t0, t1) of the cache for the G = NH/NKV query heads that share
-// the kv head; each of its 4 warps takes every 4th position with an online
+// the kv head; each of its 8 warps takes every 8th position with an online
 // softmax (lane l holds dims 4l..4l+3; two positions' loads in flight).  The
 // CTA's partial (max, sum, o) goes to the workspace; the last CTA of the kv
 // head merges the splits in split order (deterministic) and writes out, then
@@ -82,9 +83,8 @@ __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict
 // a CTA has ~32 positions, which left one warp doing all of them.)
 constexpr int kAttnSplits = 32;
 constexpr int kAttnMaxG = 8;
-constexpr int kAttnWarps = 4;
 
-template <int G>
+template <int G, int kAttnWarps>
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
     const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
@@ -319,14 +319,21 @@ extern "C" af_status af_decode_attention(const void* q, const void* k_cache, con
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     int* counters = reinterpret_cast<int*>(ws + 256);
     float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
-    const dim3 grid(kAttnSplits, n_kv_heads), block(kAttnWarps * 32);
+    static const int warps = [] {   // AF_ATTN_WARPS=4: four warps per CTA (A/B runs; 8 measured 6.5% faster per step)
+        const char* e = getenv("AF_ATTN_WARPS");
+        return (e && atoi(e) == 4) ? 4 : 8;
+    }();
+    const dim3 grid(kAttnSplits, n_kv_heads), block(warps * 32);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
                  *vh = static_cast<const __half*>(v_cache);
     __half* oh = static_cast<__half*>(out);
     switch (n_heads / n_kv_heads) {
 #define AF_ATTN(GG) \
-    case GG: attention_kernel<GG><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters); break;
+    case GG:                                                                                                  \
+        if (warps == 8) attention_kernel<GG, 8><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters); \
+        else attention_kernel<GG, 4><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters);          \
+        break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN
     }

@@ -80,6 +80,7 @@ C_SYMBOLS = {
     "af_rope_set_form": (_i, [_i]),
     "af_decode_attention_workspace_bytes": (_sz, [_i, _i]),
     "af_decode_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "af_decode_rope_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "af_rmsnorm": (_i, [_vp, _vp, ctypes.c_float, _vp, _i, _vp]),
     "af_decode_advance": (_i, [_vp, _i, _vp]),
     "af_view_last_status": (_i, []),

@@ -88,7 +88,12 @@ template <int G, int kAttnWarps>
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
     const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
-    int* __restrict__ counters) {
+    int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
+    int form, __half* k_wr, __half* v_wr) {
+    // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
+    // vector: every CTA rotates its own query heads, and the current position's
+    // k (rotated) and v come from qkv in registers; the one CTA whose range
+    // holds that position also writes them to the caches (no CTA reads that row).
     constexpr int HD = 128;
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -98,15 +103,57 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const int kv_dim = NKV * HD;
     const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
 
+    const bool fused = cos_tab != nullptr;
+    const int pos = seq - 1;
+    // RoPE of 4 dims held by this lane; dims d and d + HD/2 sit in lanes l and l ^ 16.
+    float rc[4], rs[4];
+    if (fused) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int d = (lane & 15) * 4 + e;
+            rc[e] = cos_tab[(size_t)pos * (HD / 2) + d];
+            rs[e] = sin_tab[(size_t)pos * (HD / 2) + d];
+        }
+    }
+    auto rotate = [&](float (&v)[4]) {   // v: this lane's 4 dims -> rotated, rounded to FP16
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            float o0, o1;
+            // (x, y) = (dim d, dim d + HD/2): lanes < 16 own x and keep o0, the others own y and keep o1
+            if (lane < 16) rope_pair(v[e], other, rc[e], rs[e], form, o0, o1);
+            else rope_pair(other, v[e], rc[e], rs[e], form, o0, o1);
+            v[e] = __half2float(__float2half_rn(lane < 16 ? o0 : o1));
+        }
+    };
+    auto load4 = [&](const __half* src, float (&v)[4]) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(src);
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        v[0] = __low2float(a);
+        v[1] = __high2float(a);
+        v[2] = __low2float(b);
+        v[3] = __high2float(b);
+    };
     float qv[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(q + (size_t)(kvh * G + g) * HD + lane * 4);
-        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
-        qv[g][0] = __low2float(a);
-        qv[g][1] = __high2float(a);
-        qv[g][2] = __low2float(b);
-        qv[g][3] = __high2float(b);
+        load4(q + (size_t)(kvh * G + g) * HD + lane * 4, qv[g]);
+        if (fused) rotate(qv[g]);
+    }
+    float kcur[4], vcur[4];
+    if (fused) {
+        const __half* kq = q + (size_t)NH * HD + (size_t)kvh * HD + lane * 4;
+        load4(kq, kcur);
+        rotate(kcur);
+        load4(kq + (size_t)NKV * HD, vcur);
+        if (warp == 0 && t0 <= pos && pos < t1) {
+            const size_t row = (size_t)pos * kv_dim + (size_t)kvh * HD + lane * 4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                k_wr[row + e] = __float2half_rn(kcur[e]);
+                v_wr[row + e] = __float2half_rn(vcur[e]);
+            }
+        }
     }
     float m[G], l[G], o[G][4];
 #pragma unroll
@@ -116,6 +163,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
         o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
     }
     auto load = [&](int t, float (&kf)[4], float (&vf)[4]) {
+        if (fused && t == pos) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                kf[e] = kcur[e];
+                vf[e] = vcur[e];
+            }
+            return;
+        }
         const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
         const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
         const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
@@ -306,9 +361,9 @@ extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_head
     return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_kv_heads * kAttnSplits * g * (2 + 128) * 4;
 }
 
-extern "C" af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
-                                        void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
-                                        size_t workspace_bytes, void* stream) {
+static af_status attention_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
+                                  void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
+                                  size_t workspace_bytes, void* stream, const float* cos_tab, const float* sin_tab) {
     if (q == nullptr || k_cache == nullptr || v_cache == nullptr || d_pos == nullptr || out == nullptr ||
         n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
         return AF_ERR_INVALID;
@@ -328,17 +383,39 @@ extern "C" af_status af_decode_attention(const void* q, const void* k_cache, con
     const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
                  *vh = static_cast<const __half*>(v_cache);
     __half* oh = static_cast<__half*>(out);
+    // fused RoPE mode writes the current row of the caches (the caller's buffers are writable)
+    __half* kw = cos_tab ? const_cast<__half*>(kh) : nullptr;
+    __half* vw = cos_tab ? const_cast<__half*>(vh) : nullptr;
     switch (n_heads / n_kv_heads) {
 #define AF_ATTN(GG) \
     case GG:                                                                                                  \
-        if (warps == 8) attention_kernel<GG, 8><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters); \
-        else attention_kernel<GG, 4><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters);          \
+        if (warps == 8)                                                                                       \
+            attention_kernel<GG, 8><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
+                                                            cos_tab, sin_tab, n_heads, g_rope_form, kw, vw);    \
+        else                                                                                                  \
+            attention_kernel<GG, 4><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
+                                                            cos_tab, sin_tab, n_heads, g_rope_form, kw, vw);    \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_kernel");
+}
+
+extern "C" af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
+                                        void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+    return attention_launch(q, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, workspace,
+                            workspace_bytes, stream, nullptr, nullptr);
+}
+
+extern "C" af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
+                                             void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
+                                             int head_dim, void* workspace, size_t workspace_bytes, void* stream) {
+    if (cos_tab == nullptr || sin_tab == nullptr) return AF_ERR_INVALID;
+    return attention_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, workspace,
+                            workspace_bytes, stream, cos_tab, sin_tab);
 }
 
 extern "C" af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream) {

@@ -9,8 +9,7 @@ element-wise work fused into the projections:
   embedding lookup                        af_embed_lookup
   per layer:
     RMSNorm + QKV                         af_rmsnorm_w8a16_gemv
-    RoPE + KV-cache write                 af_rope_kv_write
-    cached GQA attention                  af_decode_attention
+    RoPE + KV-cache write + attention     af_decode_rope_attention
     O + residual                          af_w8a16_gemv_residual
     RMSNorm + gate/up + SwiGLU            af_rmsnorm_w8a16_swiglu
     down + residual                       af_w8a16_gemv_residual
@@ -145,11 +144,9 @@ class DecodeEngine:
             wq, sq = ly["qkv"]
             check(L.af_rmsnorm_w8a16_gemv(p(self.x), p(ly["in_norm"]), NORM_EPS, p(wq), p(sq), p(self.qkv),
                                           self.QD + 2 * self.KVD, self.D, 128, 0, None, st), "rmsnorm_gemv")
-            check(L.af_rope_kv_write(p(self.qkv), p(self.cos), p(self.sin), p(self.d_pos), p(ly["k_cache"]),
-                                     p(ly["v_cache"]), self.NH, self.NKV, self.HD, st), "rope_kv_write")
-            check(L.af_decode_attention(p(self.qkv), p(ly["k_cache"]), p(ly["v_cache"]), p(self.d_pos),
-                                        p(self.attn), self.NH, self.NKV, self.HD, p(self.attn_ws),
-                                        self.attn_ws.numel(), st), "decode_attention")
+            check(L.af_decode_rope_attention(p(self.qkv), p(self.cos), p(self.sin), p(self.d_pos), p(ly["k_cache"]),
+                                             p(ly["v_cache"]), p(self.attn), self.NH, self.NKV, self.HD,
+                                             p(self.attn_ws), self.attn_ws.numel(), st), "rope_attention")
             wo, so = ly["o"]
             check(L.af_w8a16_gemv_residual(p(self.attn), p(wo), p(so), p(self.x), self.D, self.QD, 128, 0, None, st),
                   "o + residual")
@@ -159,7 +156,7 @@ class DecodeEngine:
             wd, sd = ly["down"]
             check(L.af_w8a16_gemv_residual(p(self.h), p(wd), p(sd), p(self.x), self.D, self.FFN, 128, 0, None, st),
                   "down + residual")
-            n += 6
+            n += 5
         check(L.af_rmsnorm(p(self.x), p(self.final_norm), NORM_EPS, p(self.xn), self.D, st), "final rmsnorm")
         check(L.af_lm_head_gemv(p(self.xn), p(self.lm_head), 0, None, p(self.logits), self.V, self.D,
                                 p(self.d_token), self.mode, p(self.lm_ws), self.lm_ws.numel(), st), "lm_head")

@@ -204,6 +204,12 @@ size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads);
 af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos, void* out,
                               int n_heads, int n_kv_heads, int head_dim, void* workspace, size_t workspace_bytes,
                               void* stream);
+/* RoPE + KV-cache write + attention in one launch: q, k, v read from the raw qkv vector; the same
+ * results, bit for bit, as af_rope_kv_write followed by af_decode_attention (qkv itself is left
+ * unrotated). */
+af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
+                                   void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
+                                   int head_dim, void* workspace, size_t workspace_bytes, void* stream);
 af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream);
 af_status af_decode_advance(int* d_pos, int by, void* stream);
 

@@ -157,6 +157,38 @@ def test_decode_attention_parity():
             assert ok.all(), f"{name} pos {pos}: {int((~ok).sum())} outputs off, max err {err.max():.3g}"
 
 
+def test_fused_rope_attention_equals_the_two_kernels():
+    L = lib()
+    cos, sin = _tables()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(17)
+    qd, kvd = NH * HD, NKV * HD
+    ws_a = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV), dtype=torch.uint8, device="cuda")
+    ws_b = torch.zeros_like(ws_a)
+    kc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
+    vc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
+    for pos in (0, 1, 33, 1024, 2047):
+        qkv = (torch.randn(qd + 2 * kvd, generator=g, device="cuda") * 2).half()
+        dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        ka, va, kb, vb = kc.clone(), vc.clone(), kc.clone(), vc.clone()
+        oa = torch.zeros(qd, dtype=torch.float16, device="cuda")
+        ob = torch.zeros_like(oa)
+        a = qkv.clone()
+        assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), ka.data_ptr(),
+                                  va.data_ptr(), NH, NKV, HD, st()) == 0
+        assert L.af_decode_attention(a.data_ptr(), ka.data_ptr(), va.data_ptr(), dpos.data_ptr(), oa.data_ptr(), NH,
+                                     NKV, HD, ws_a.data_ptr(), ws_a.numel(), st()) == 0
+        b = qkv.clone()
+        assert L.af_decode_rope_attention(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kb.data_ptr(),
+                                          vb.data_ptr(), ob.data_ptr(), NH, NKV, HD, ws_b.data_ptr(), ws_b.numel(),
+                                          st()) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(oa.view(torch.int16), ob.view(torch.int16)), pos
+        assert torch.equal(ka.view(torch.int16), kb.view(torch.int16)), pos
+        assert torch.equal(va.view(torch.int16), vb.view(torch.int16)), pos
+        assert torch.equal(b, qkv)   # the fused kernel leaves qkv unrotated
+
+
 def test_decode_engine_tokens_match_reference(tmp_path):
     R = oracle.ref_engine()
     if R is None:

@@ -513,7 +513,7 @@ def run_decode(args, device, local):
     config = {"workload": "llama3.2-3b-shaped greedy decode, 28 layers, random-init weights in the reference .bin "
                           "format (BASELINE config 3)", "position": DECODE_POS, "M": 1,
               "kv_cache": f"prefilled to {DECODE_POS} positions by teacher-forced steps (seeded random tokens)",
-              "l2": "5.2 GB of weights per step >> 126 MB L2 (no flush needed)", "parallelism": "single"}
+              "l2": "3.8 GB read per step (weights, lm_head, KV cache) >> 126 MB L2 (no flush needed)", "parallelism": "single"}
     out = {"metric": "decode tok/s (Llama-3.2-3B-shaped, M=1, KV cache at 1024 positions)", "unit": "tok/s",
            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "fp8e4m3 weights x fp16 act, fp32 accum", "data": "synthetic seeded",

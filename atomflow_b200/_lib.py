@@ -77,7 +77,6 @@ C_SYMBOLS = {
     "af_embed_lookup": (_i, [_vp, _vp, _vp, _i, _vp]),
     "af_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float]),
     "af_rope_kv_write": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
-    "af_rope_set_form": (_i, [_i]),
     "af_decode_attention_workspace_bytes": (_sz, [_i, _i]),
     "af_decode_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "af_decode_rope_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),

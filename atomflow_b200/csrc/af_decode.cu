@@ -311,7 +311,10 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const __half* __restrict__
 
 __global__ void advance_kernel(int* d_pos, int by) { *d_pos += by; }
 
-int g_rope_form = 0;   // operand order of the RoPE contraction (see rope_pair)
+// Operand order of the RoPE contraction (see rope_pair): form 0 reproduces the
+// reference's rope kernel bit for bit (tests/test_decode_gpu.py pins it; form 1
+// is the other order, kept in rope_pair for that comparison).
+constexpr int kRopeForm = 0;
 
 }  // namespace
 
@@ -344,16 +347,11 @@ extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const flo
         return AF_ERR_INVALID;
     rope_kv_kernel<<<n_heads + n_kv_heads, 64, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<__half*>(qkv), cos_tab, sin_tab, d_pos, static_cast<__half*>(k_cache),
-        static_cast<__half*>(v_cache), n_heads, n_kv_heads, head_dim, g_rope_form);
+        static_cast<__half*>(v_cache), n_heads, n_kv_heads, head_dim, kRopeForm);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "rope_kv_kernel");
 }
 
-extern "C" af_status af_rope_set_form(int form) {
-    if (form != 0 && form != 1) return AF_ERR_INVALID;
-    g_rope_form = form;
-    return AF_OK;
-}
 
 extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads) {
     if (n_kv_heads <= 0 || n_heads % n_kv_heads) return 0;
@@ -391,10 +389,10 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     case GG:                                                                                                  \
         if (warps == 8)                                                                                       \
             attention_kernel<GG, 8><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
-                                                            cos_tab, sin_tab, n_heads, g_rope_form, kw, vw);    \
+                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw);    \
         else                                                                                                  \
             attention_kernel<GG, 4><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
-                                                            cos_tab, sin_tab, n_heads, g_rope_form, kw, vw);    \
+                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw);    \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN

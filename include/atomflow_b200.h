@@ -193,13 +193,11 @@ af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const v
  *                        it zeroed.  (tiled_attention.cu gqa_cached_attention_kernel)
  *   af_rmsnorm           the reference's rms_norm arithmetic, one vector
  *   af_decode_advance    *d_pos += by (the step's last launch)
- * af_rope_set_form picks the operand order of RoPE's fused multiply-add (0 or
- * 1), kept for the parity test that pins it against the reference kernel. */
+ */
 af_status af_embed_lookup(const float* table, const int* d_token, void* x, int D, void* stream);
 af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq, int head_dim, float base);
 af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos, void* k_cache,
                            void* v_cache, int n_heads, int n_kv_heads, int head_dim, void* stream);
-af_status af_rope_set_form(int form);
 size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads);
 af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos, void* out,
                               int n_heads, int n_kv_heads, int head_dim, void* workspace, size_t workspace_bytes,

@@ -67,27 +67,22 @@ def test_rope_kv_write_matches_reference():
     g = torch.Generator(device="cuda")
     g.manual_seed(4)
     qd, kvd = NH * HD, NKV * HD
-    matches = {}
-    for form in (0, 1):
-        assert L.af_rope_set_form(form) == 0
-        ok = True
-        for pos in (0, 5, 1000, 2047):
-            qkv = (torch.randn(qd + 2 * kvd, generator=g, device="cuda") * 3).half()
-            a, b = qkv.clone(), qkv.clone()
-            kc_a = torch.zeros(MAXSEQ, kvd, dtype=torch.float16, device="cuda")
-            vc_a, kc_b, vc_b = kc_a.clone(), kc_a.clone(), kc_a.clone()
-            dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
-            assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kc_a.data_ptr(),
-                                      vc_a.data_ptr(), NH, NKV, HD, st()) == 0
-            assert ref().afref_rope_kv(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), kc_b.data_ptr(), vc_b.data_ptr(),
-                                       pos, NH, NKV, HD, st()) == 0
-            torch.cuda.synchronize()
-            ok &= torch.equal(a.view(torch.int16), b.view(torch.int16))
-            ok &= torch.equal(kc_a.view(torch.int16), kc_b.view(torch.int16))
-            ok &= torch.equal(vc_a.view(torch.int16), vc_b.view(torch.int16))
-        matches[form] = ok
-    assert L.af_rope_set_form(0) == 0
-    assert matches[0], f"RoPE differs from the reference kernel (form 0); form 1 matches: {matches[1]}"
+    ok = True
+    for pos in (0, 5, 1000, 2047):
+        qkv = (torch.randn(qd + 2 * kvd, generator=g, device="cuda") * 3).half()
+        a, b = qkv.clone(), qkv.clone()
+        kc_a = torch.zeros(MAXSEQ, kvd, dtype=torch.float16, device="cuda")
+        vc_a, kc_b, vc_b = kc_a.clone(), kc_a.clone(), kc_a.clone()
+        dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kc_a.data_ptr(),
+                                  vc_a.data_ptr(), NH, NKV, HD, st()) == 0
+        assert ref().afref_rope_kv(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), kc_b.data_ptr(), vc_b.data_ptr(),
+                                   pos, NH, NKV, HD, st()) == 0
+        torch.cuda.synchronize()
+        ok &= torch.equal(a.view(torch.int16), b.view(torch.int16))
+        ok &= torch.equal(kc_a.view(torch.int16), kc_b.view(torch.int16))
+        ok &= torch.equal(vc_a.view(torch.int16), vc_b.view(torch.int16))
+    assert ok, "RoPE + KV write differs from the reference kernels"
 
 
 def test_embed_and_rmsnorm_match_reference():

@@ -16,15 +16,6 @@ element-wise work fused into the projections:
   final RMSNorm                           af_rmsnorm
   lm_head (FP16) + greedy argmax          af_lm_head_gemv
 
-Tensor parallelism (rank/world, one process per GPU): QKV split by heads
-(each rank holds its query heads and their kv heads, repacked [Q_r | K_r | V_r]),
-gate/up split by rows, O and down split along K and summed over the ranks
-inside the projection kernel with the residual folded in
-(af_w8a16_gemv_allreduce_residual), the lm_head split by vocabulary rows with
-the argmax pairs exchanged inside its kernel (af_lm_head_gemv_tp) -- every rank
-ends the step holding the same token.  Norms, embedding and position are
-replicated.
-
 The token id and the position are device ints: `forward_pass` launches one
 step eagerly; `capture()` records one step (optionally followed by the
 position increment) as a CUDA graph whose replays generate token after token
@@ -46,52 +37,16 @@ ROPE_BASE = 500000.0
 MAX_SEQ_LEN = 2048   # the reference engine's static KV cache length (engine.h:22)
 
 
-def shard_linear(name, q, s, shape, rank, world):
-    """This rank's part of projection `name` (q: FP8 [N, K], s: FP16-bit group
-    scales [N, K/128], numpy) under tensor parallelism of `world` ranks."""
-    if world == 1:
-        return q, s
-    nh, nkv, hd, g = shape.n_heads, shape.n_kv_heads, shape.head_dim, 128
-    if nh % world or nkv % world:
-        raise ValueError(f"{nh} query / {nkv} kv heads do not split over {world} ranks")
-    if name == "qkv":
-        hq, hk = nh // world, nkv // world
-        parts = [slice(rank * hq * hd, (rank + 1) * hq * hd),
-                 slice(nh * hd + rank * hk * hd, nh * hd + (rank + 1) * hk * hd),
-                 slice((nh + nkv) * hd + rank * hk * hd, (nh + nkv) * hd + (rank + 1) * hk * hd)]
-        return np.concatenate([q[p] for p in parts]), np.concatenate([s[p] for p in parts])
-    if name in ("gate", "up"):
-        n = q.shape[0]
-        if n % world:
-            raise ValueError(f"{name}: {n} rows do not split over {world} ranks")
-        r = slice(rank * n // world, (rank + 1) * n // world)
-        return q[r], s[r]
-    # o, down: split along K on whole scale groups (o: the rank's heads' dims)
-    k = q.shape[1]
-    if k % (g * world):
-        raise ValueError(f"{name}: K={k} does not split into 128-wide groups over {world} ranks")
-    c = slice(rank * k // world, (rank + 1) * k // world)
-    cg = slice(rank * k // world // g, (rank + 1) * k // world // g)
-    return q[:, c], s[:, cg]
-
-
 class DecodeEngine:
-    def __init__(self, path, device="cuda", max_seq_len=MAX_SEQ_LEN, true_argmax=False, rank=0, world=1,
-                 group=None):
+    def __init__(self, path, device="cuda", max_seq_len=MAX_SEQ_LEN, true_argmax=False):
         self.L = lib()
-        self.rank, self.world = rank, world
         self.dev = torch.device(device)
         self.mode = 0 if true_argmax else 1
         b = BinFile(path)
         s = self.shape = b.shape
         self.D, self.FFN, self.V, self.NL = s.dim, s.ffn, s.vocab, s.n_layers
-        if s.n_heads % world or s.n_kv_heads % world or s.ffn % (128 * world):
-            raise ValueError(f"the model does not split over {world} ranks")
-        # local (per-rank) head counts and widths
-        self.NH, self.NKV, self.HD = s.n_heads // world, s.n_kv_heads // world, s.head_dim
+        self.NH, self.NKV, self.HD = s.n_heads, s.n_kv_heads, s.head_dim
         self.QD, self.KVD = self.NH * self.HD, self.NKV * self.HD
-        self.FFN_l = s.ffn // world
-        self.v0, self.v1 = rank * s.vocab // world, (rank + 1) * s.vocab // world
         self.max_seq = max_seq_len
 
         def up(a, dt=None):
@@ -105,13 +60,13 @@ class DecodeEngine:
         for i in range(self.NL):
             ly = {"in_norm": up(b.block(f"layers.{i}.input_norm")), "post_norm": up(b.block(f"layers.{i}.post_norm"))}
             for name, _, _ in s.linears():
-                q, sc = shard_linear(name, *b.linear(i, name), s, rank, world)
+                q, sc = b.linear(i, name)
                 ly[name] = (up(q), up(sc.view(np.int16)))
             ly["k_cache"] = torch.zeros(max_seq_len, self.KVD, dtype=torch.float16, device=self.dev)
             ly["v_cache"] = torch.zeros(max_seq_len, self.KVD, dtype=torch.float16, device=self.dev)
             self.layers.append(ly)
         self.final_norm = up(b.block("final_norm"))
-        self.lm_head = up(b.block("lm_head")[self.v0:self.v1].view(np.int16))
+        self.lm_head = up(b.block("lm_head").view(np.int16))
         b.close()
 
         cos = np.empty((max_seq_len, self.HD // 2), np.float32)
@@ -123,20 +78,16 @@ class DecodeEngine:
         z = lambda n, dt=torch.float16: torch.zeros(n, dtype=dt, device=self.dev)  # noqa: E731
         self.x, self.xn = z(self.D), z(self.D)
         self.qkv, self.attn = z(self.QD + 2 * self.KVD), z(self.QD)
-        self.h = z(self.FFN_l)
-        self.logits = z(self.v1 - self.v0, torch.float32)
+        self.h = z(self.FFN)
+        self.logits = z(self.V, torch.float32)
         self.d_token = z(1, torch.int32)
         self.d_pos = z(1, torch.int32)
         aw = self.L.af_decode_attention_workspace_bytes(self.NH, self.NKV)
         self.attn_ws = z(aw, torch.uint8)
-        lw = self.L.af_lm_head_workspace_bytes(self.v1 - self.v0, self.D, 0)
+        lw = self.L.af_lm_head_workspace_bytes(self.V, self.D, 0)
         self.lm_ws = z(lw, torch.uint8)
         self.stream = torch.cuda.Stream(self.dev)
         self.stream.wait_stream(torch.cuda.current_stream(self.dev))   # the uploads above
-        self.comm = None
-        if world > 1:
-            from .tp import TpComm
-            self.comm = TpComm(rank, world, self.D, group)
 
     # ---- the reference engine's interface
     # (host reads and writes of the device ints go through the engine's stream,
@@ -196,46 +147,32 @@ class DecodeEngine:
             check(L.af_decode_rope_attention(p(self.qkv), p(self.cos), p(self.sin), p(self.d_pos), p(ly["k_cache"]),
                                              p(ly["v_cache"]), p(self.attn), self.NH, self.NKV, self.HD,
                                              p(self.attn_ws), self.attn_ws.numel(), st), "rope_attention")
-            self._row_residual(ly["o"], self.attn, self.QD, st)
+            wo, so = ly["o"]
+            check(L.af_w8a16_gemv_residual(p(self.attn), p(wo), p(so), p(self.x), self.D, self.QD, 128, 0, None, st),
+                  "o + residual")
             (wg, sg), (wu, su) = ly["gate"], ly["up"]
             check(L.af_rmsnorm_w8a16_swiglu(p(self.x), p(ly["post_norm"]), NORM_EPS, p(wg), p(sg), p(wu), p(su),
-                                            p(self.h), self.FFN_l, self.D, 128, 0, None, None, st), "rmsnorm_swiglu")
-            self._row_residual(ly["down"], self.h, self.FFN_l, st)
+                                            p(self.h), self.FFN, self.D, 128, 0, None, None, st), "rmsnorm_swiglu")
+            wd, sd = ly["down"]
+            check(L.af_w8a16_gemv_residual(p(self.h), p(wd), p(sd), p(self.x), self.D, self.FFN, 128, 0, None, st),
+                  "down + residual")
             n += 5
         check(L.af_rmsnorm(p(self.x), p(self.final_norm), NORM_EPS, p(self.xn), self.D, st), "final rmsnorm")
-        if self.comm is None:
-            check(L.af_lm_head_gemv(p(self.xn), p(self.lm_head), 0, None, p(self.logits), self.V, self.D,
-                                    p(self.d_token), self.mode, p(self.lm_ws), self.lm_ws.numel(), st), "lm_head")
-        else:   # vocab-parallel: every rank ends with the same global token
-            check(L.af_lm_head_gemv_tp(p(self.xn), p(self.lm_head), 0, None, p(self.logits), self.v1 - self.v0,
-                                       self.D, self.v0, p(self.d_token), self.mode, p(self.lm_ws),
-                                       self.lm_ws.numel(), self.comm.h, st), "lm_head_tp")
+        check(L.af_lm_head_gemv(p(self.xn), p(self.lm_head), 0, None, p(self.logits), self.V, self.D,
+                                p(self.d_token), self.mode, p(self.lm_ws), self.lm_ws.numel(), st), "lm_head")
         n += 2
         if advance:
             check(L.af_decode_advance(p(self.d_pos), 1, st), "advance")
             n += 1
         self.launches_per_step = n
 
-    def _row_residual(self, wsc, x_in, K, st):
-        """x += W x_in for a row-split projection (O, down): summed over the
-        ranks inside the kernel when tensor-parallel."""
-        L, p = self.L, (lambda t: t.data_ptr())
-        w, sc = wsc
-        if self.comm is None:
-            check(L.af_w8a16_gemv_residual(p(x_in), p(w), p(sc), p(self.x), self.D, K, 128, 0, None, st),
-                  "gemv + residual")
-        else:
-            check(L.af_w8a16_gemv_allreduce_residual(p(x_in), p(w), p(sc), p(self.x), self.D, K, 128, 0,
-                                                     self.comm.h, st), "gemv + all-reduce + residual")
-
     def weight_bytes(self) -> int:
         """Bytes a step must read at least: every weight, scale and norm, the
         embedding row, and the KV cache up to the current position."""
         s = self.shape
-        b = sum(n * k + n * (k // 128) * 2 for _, n, k in s.linears()) * self.NL // self.world
-        b += (2 * self.D * 4) * self.NL + self.D * 4 + (self.v1 - self.v0) * self.D * 2 + self.D * 4
+        b = sum(n * k + n * (k // 128) * 2 for _, n, k in s.linears()) * self.NL
+        b += (2 * self.D * 4) * self.NL + self.D * 4 + self.V * self.D * 2 + self.D * 4
         return b
 
     def kv_bytes(self, pos: int) -> int:
-        """This rank's KV-cache bytes read at position `pos`."""
         return 2 * (pos + 1) * self.KVD * 2 * self.NL

@@ -499,21 +499,16 @@ def decode_model_path():
     return path
 
 
-def run_decode(args, device, local, rank=0, world=1, dist_on=False):
+def run_decode(args, device, local):
     """Greedy decode of a Llama-3.2-3B-shaped model (config 3): KV cache
     prefilled to 1024 positions by teacher-forced steps with seeded random
     tokens, then `steps` greedy steps.  Ours: DecodeEngine, one CUDA-graph
     replay per token, position and token kept on the device.  Reference: its
     own AtomFlowEngine (oracle/_ref), TPOT as its main.cu measures it -- one
     graph of forward_pass at position 1024, replayed."""
-    if rank == 0:
-        path = decode_model_path()
-    if dist_on:
-        torch.distributed.barrier()   # rank 0 has written the model file
     path = decode_model_path()
-    sampler = ClockSampler(local) if rank == 0 else None
-    if sampler:
-        sampler.wait_first()
+    sampler = ClockSampler(local)
+    sampler.wait_first()
     peak, peak_kind = measured_peaks()
     config = {"workload": "llama3.2-3b-shaped greedy decode, 28 layers, random-init weights in the reference .bin "
                           "format (BASELINE config 3)", "position": DECODE_POS, "M": 1,
@@ -546,12 +541,7 @@ def run_decode(args, device, local, rank=0, world=1, dist_on=False):
         print(json.dumps(out))
         os._exit(0)
     from atomflow_b200.decode import DecodeEngine
-    eng = DecodeEngine(path, rank=rank, world=world)
-    if world > 1:
-        config["parallelism"] = (f"tp{world}: heads, gate/up rows and vocab split; O/down summed over NVLink "
-                                 "inside their kernels; the argmax exchanged inside the lm_head kernel")
-        out["n_gpus"] = world
-        out["scaling"] = "strong"
+    eng = DecodeEngine(path)
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, 65536, DECODE_POS).tolist()
     g = eng.capture(advance=True)
@@ -570,8 +560,6 @@ def run_decode(args, device, local, rank=0, world=1, dist_on=False):
     eng.current_pos = DECODE_POS
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     eng.stream.synchronize()
-    if dist_on:
-        torch.distributed.barrier()
     t0 = time.time()
     ev0.record(eng.stream)
     for _ in range(args.steps):
@@ -580,11 +568,7 @@ def run_decode(args, device, local, rank=0, world=1, dist_on=False):
     eng.stream.synchronize()
     t1 = time.time()
     ms = ev0.elapsed_time(ev1) / args.steps
-    if dist_on:   # the slowest rank's time
-        tms = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(tms, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tms.item())
-    clocks = sampler.summary(t0, t1) if sampler else None
+    clocks = sampler.summary(t0, t1)
     # end to end: each step the host sends the token and reads the next one (pinned, inside the graph)
     tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
     tok_back = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -606,14 +590,7 @@ def run_decode(args, device, local, rank=0, world=1, dist_on=False):
     ev1.record(eng.stream)
     eng.stream.synchronize()
     e2e_ms = ev0.elapsed_time(ev1) / args.steps
-    if dist_on:
-        tms = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(tms, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(tms.item())
-    if sampler:
-        sampler.stop()
-    if eng.comm is not None and eng.comm.status() != 0:
-        raise RuntimeError("a tensor-parallel peer wait ran out (status word set)")
+    sampler.stop()
     step_bytes = eng.weight_bytes() + eng.kv_bytes(DECODE_POS + args.steps // 2)
     achieved = step_bytes / (ms / 1e3) / 1e9
     out.update({"value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 5), "clocks": clocks,
@@ -628,9 +605,8 @@ def run_decode(args, device, local, rank=0, world=1, dist_on=False):
                         "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                         "path": "DecodeEngine over the C ABI: token H2D from pinned memory, the step, next token D2H "
                                 "to pinned memory, one CUDA graph per step"}})
-    if rank == 0:
-        print(json.dumps(out))
-    finish(dist_on)
+    print(json.dumps(out))
+    os._exit(0)
 
 
 def main():
@@ -664,7 +640,9 @@ def main():
 
     wl = args.workload
     if wl == "decode":
-        return run_decode(args, device, local, rank, world if dist_on else 1, dist_on)
+        if world > 1:
+            raise SystemExit("the decode workload runs on one GPU")
+        return run_decode(args, device, local)
     if wl == "layerset":
         items = make_layerset(device, trank, tp, layers=args.layers)
         config = {"workload": f"llama3.2-3b layer-set x{args.layers} (BASELINE config 1)", "M": 1,

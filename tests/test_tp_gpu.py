@@ -240,57 +240,3 @@ def test_lm_head_tp_missing_peer_times_out_with_status():
     assert status.value & 1
     assert 0 <= int(idx.item()) < V   # the local candidate survives a missing peer
     assert L.af_tp_destroy(h) == 0
-
-
-def _decode_rank_main(rank, world, port, out_q, path):
-    import torch.distributed as dist
-    from atomflow_b200.decode import DecodeEngine
-    torch.cuda.set_device(rank)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
-    eng = DecodeEngine(path, rank=rank, world=world)
-    prompt = np.random.default_rng(5).integers(0, 65536, 16).tolist()
-
-    def run(e):
-        seq, tok = [], None
-        for pos in range(16 + 32):
-            e.current_pos = pos
-            e.inject_token(prompt[pos] if pos < 16 else tok)
-            e.forward_pass()
-            tok = e.get_output_token()
-            if pos >= 15:
-                seq.append(tok)
-        return seq
-
-    mine = run(eng)
-    assert eng.comm.status() == 0
-    seqs = [None] * world
-    dist.all_gather_object(seqs, mine)
-    if rank == 0:
-        single = run(DecodeEngine(path))   # the same model on one GPU
-        same = sum(a == b for a, b in zip(single, mine))
-        print(f"TP{world} decode: {same} of {len(mine)} tokens equal to the one-GPU engine")
-        assert all(sq == seqs[0] for sq in seqs), "ranks disagree"
-        assert mine == single
-        out_q.put("ok")
-    dist.barrier()
-    os._exit(0)
-
-
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_decode_engine_tensor_parallel_two_gpus(tmp_path):
-    from atomflow_b200.weights_bin import ModelShape, write_synthetic_bin
-    path = tmp_path / "tiny.bin"
-    write_synthetic_bin(path, ModelShape(dim=1024, ffn=2048, n_layers=4, n_heads=8, n_kv_heads=2, vocab=128256,
-                                         max_seq_len=2048), seed=21)
-    import torch.multiprocessing as mp
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    ps = [ctx.Process(target=_decode_rank_main, args=(r, 2, port, q, str(path))) for r in range(2)]
-    for p in ps:
-        p.start()
-    for p in ps:
-        p.join(timeout=300)
-    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
-    assert q.get(timeout=5) == "ok"

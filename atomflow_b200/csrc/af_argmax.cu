@@ -136,15 +136,6 @@ int device_sm_count(int* device_out) {
     return cache[dev];
 }
 
-int ctas_per_sm() {
-    static int v = [] {
-        const char* e = getenv("AF_CTAS_PER_SM");
-        int k = e ? atoi(e) : 1;
-        return (k >= 1 && k <= 4) ? k : 1;
-    }();
-    return v;
-}
-
 }  // namespace af
 
 using namespace af;
@@ -163,7 +154,17 @@ extern "C" const char* af_status_string(af_status s) {
 
 extern "C" const char* af_last_cuda_error(void) { return g_cuda_err; }
 
-extern "C" int af_version(void) { return 100; }
+extern "C" int af_version(void) { return 110; }
+
+extern "C" af_status af_device_faults(unsigned* out, int clear) {
+    if (out == nullptr) return AF_ERR_INVALID;
+    cudaError_t e1 = cudaSuccess, e2 = cudaSuccess;
+    const unsigned v = gemv_faults(clear != 0, &e1) | decode_faults(clear != 0, &e2);
+    if (e1 != cudaSuccess) return cuda_fail(e1, "af_device_faults");
+    if (e2 != cudaSuccess) return cuda_fail(e2, "af_device_faults");
+    *out = v;
+    return AF_OK;
+}
 
 extern "C" af_status af_workspace_reset(void* workspace, size_t workspace_bytes, void* stream) {
     if (workspace == nullptr) return workspace_bytes == 0 ? AF_OK : AF_ERR_INVALID;

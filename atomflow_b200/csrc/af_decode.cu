@@ -18,7 +18,18 @@
 
 using namespace af;
 
+// Fault bits (AF_FAULT_*) of this device's decode kernels, read by af_device_faults.
+__device__ unsigned int g_decode_faults;
+
 namespace {
+
+// A position outside the KV cache: record it once and skip the launch's work
+// (every CTA sees the same *d_pos, so all of them return).
+__device__ __forceinline__ bool pos_out_of_range(int pos, int max_seq) {
+    if (pos >= 0 && pos < max_seq) return false;
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) atomicOr(&g_decode_faults, (unsigned)AF_FAULT_POSITION);
+    return true;
+}
 
 // ---------------------------------------------------------------- embedding
 // x[i] = half(table[token * D + i])  (helpers.cu k_embed_lookup_kernel)
@@ -48,8 +59,9 @@ __device__ __forceinline__ void rope_pair(float x, float y, float c, float s, in
 __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict__ cos_tab,
                                const float* __restrict__ sin_tab, const int* __restrict__ d_pos,
                                __half* __restrict__ k_cache, __half* __restrict__ v_cache, int NH, int NKV, int HD,
-                               int form) {
+                               int form, int max_seq) {
     const int pos = *d_pos;
+    if (pos_out_of_range(pos, max_seq)) return;
     const int h = blockIdx.x, half_hd = HD / 2;
     const int q_dim = NH * HD, kv_dim = NKV * HD;
     for (int d = threadIdx.x; d < half_hd; d += blockDim.x) {
@@ -89,7 +101,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
     const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
     int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
-    int form, __half* k_wr, __half* v_wr) {
+    int form, __half* k_wr, __half* v_wr, int max_seq) {
     // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
     // vector: every CTA rotates its own query heads, and the current position's
     // k (rotated) and v come from qkv in registers; the one CTA whose range
@@ -97,6 +109,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
     constexpr int HD = 128;
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (pos_out_of_range(*d_pos, max_seq)) return;
     const int seq = *d_pos + 1;
     const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
     const int t0 = min(seq, split * chunk), t1 = min(seq, t0 + chunk);
@@ -341,13 +354,14 @@ extern "C" af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq,
 
 extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                      void* k_cache, void* v_cache, int n_heads, int n_kv_heads, int head_dim,
-                                     void* stream) {
+                                     int max_seq, void* stream) {
+    if (max_seq <= 0) return AF_ERR_INVALID;
     if (qkv == nullptr || cos_tab == nullptr || sin_tab == nullptr || d_pos == nullptr || k_cache == nullptr ||
         v_cache == nullptr || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || head_dim % 2)
         return AF_ERR_INVALID;
     rope_kv_kernel<<<n_heads + n_kv_heads, 64, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<__half*>(qkv), cos_tab, sin_tab, d_pos, static_cast<__half*>(k_cache),
-        static_cast<__half*>(v_cache), n_heads, n_kv_heads, head_dim, kRopeForm);
+        static_cast<__half*>(v_cache), n_heads, n_kv_heads, head_dim, kRopeForm, max_seq);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "rope_kv_kernel");
 }
@@ -360,8 +374,9 @@ extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_head
 }
 
 static af_status attention_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
-                                  void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
+                                  void* out, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* workspace,
                                   size_t workspace_bytes, void* stream, const float* cos_tab, const float* sin_tab) {
+    if (max_seq <= 0) return AF_ERR_INVALID;
     if (q == nullptr || k_cache == nullptr || v_cache == nullptr || d_pos == nullptr || out == nullptr ||
         n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
         return AF_ERR_INVALID;
@@ -372,10 +387,7 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     int* counters = reinterpret_cast<int*>(ws + 256);
     float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
-    static const int warps = [] {   // AF_ATTN_WARPS=4: four warps per CTA (A/B runs; 8 measured 6.5% faster per step)
-        const char* e = getenv("AF_ATTN_WARPS");
-        return (e && atoi(e) == 4) ? 4 : 8;
-    }();
+    constexpr int warps = 8;
     const dim3 grid(kAttnSplits, n_kv_heads), block(warps * 32);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
@@ -387,12 +399,8 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     switch (n_heads / n_kv_heads) {
 #define AF_ATTN(GG) \
     case GG:                                                                                                  \
-        if (warps == 8)                                                                                       \
-            attention_kernel<GG, 8><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
-                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw);    \
-        else                                                                                                  \
-            attention_kernel<GG, 4><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,  \
-                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw);    \
+        attention_kernel<GG, warps><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,    \
+                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw, max_seq); \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN
@@ -402,17 +410,18 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
 }
 
 extern "C" af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
-                                        void* out, int n_heads, int n_kv_heads, int head_dim, void* workspace,
-                                        size_t workspace_bytes, void* stream) {
-    return attention_launch(q, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, workspace,
+                                        void* out, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+    return attention_launch(q, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, max_seq, workspace,
                             workspace_bytes, stream, nullptr, nullptr);
 }
 
 extern "C" af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                              void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
-                                             int head_dim, void* workspace, size_t workspace_bytes, void* stream) {
+                                             int head_dim, int max_seq, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
     if (cos_tab == nullptr || sin_tab == nullptr) return AF_ERR_INVALID;
-    return attention_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, workspace,
+    return attention_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, max_seq, workspace,
                             workspace_bytes, stream, cos_tab, sin_tab);
 }
 
@@ -430,4 +439,15 @@ extern "C" af_status af_decode_advance(int* d_pos, int by, void* stream) {
     advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(d_pos, by);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "advance_kernel");
+}
+
+unsigned af::decode_faults(bool clear, cudaError_t* err) {
+    unsigned v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_decode_faults, sizeof(v));
+    if (e == cudaSuccess && clear && v != 0) {
+        const unsigned z = 0;
+        e = cudaMemcpyToSymbol(g_decode_faults, &z, sizeof(z));
+    }
+    *err = e;
+    return v;
 }

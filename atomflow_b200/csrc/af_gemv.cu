@@ -95,16 +95,6 @@ __device__ __forceinline__ uint32_t u4w(const uint4& v, int t) {
     return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
 }
 
-#ifdef AF_EXP_TRACE
-__device__ unsigned long long g_trace[64][160][6];
-__device__ long long g_trace_clk[64][160][6];
-__device__ unsigned int g_trace_launch;
-#define TRACE(k) do { if (threadIdx.x == 0 && blockIdx.x < 160) { g_trace_clk[s_tl % 64][blockIdx.x][k] = clock64(); g_trace[s_tl % 64][blockIdx.x][k] = globaltimer_ns(); } } while (0)
-extern "C" void af_exp_trace_read(unsigned long long* dst) { cudaMemcpyFromSymbol(dst, g_trace, sizeof(g_trace)); }
-extern "C" void af_exp_trace_clk(long long* dst) { cudaMemcpyFromSymbol(dst, g_trace_clk, sizeof(g_trace_clk)); }
-#else
-#define TRACE(k) do {} while (0)
-#endif
 
 // Owner of chunk `c` of a range of `n` chunks split into `parts` equal
 // contiguous pieces (parts <= n): the largest i with floor(i*n/parts) <= c.
@@ -121,12 +111,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     constexpr int XU4 = LPOS / 8;                  // uint4 of x per lane per chunk
     constexpr int PF = 4 * NT;                     // partial floats per lane
 
-#ifdef AF_EXP_TRACE
-    __shared__ unsigned s_tl;
-    if (threadIdx.x == 0) s_tl = atomicAdd(&g_trace_launch, 1) / gridDim.x;
-    __syncthreads();
-#endif
-    TRACE(0);
     pdl_launch_dependents();
     extern __shared__ __align__(128) unsigned char smem[];
     // [ring: kWarps x kS chunk slots of 1 KB][x: xs_bytes][scales: sc_bytes][warp partials]
@@ -204,7 +188,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     // Everything above touched only weights.  From here on we read the
     // activations and write outputs, which the previous kernel may own.
     pdl_wait();
-    TRACE(1);
 
     if (p.xs_stride > 0) {
         const int k8 = p.K >> 3;
@@ -217,7 +200,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
     }
     cp_async_wait<kS>();   // the scale group (the oldest) has landed
     __syncthreads();
-    TRACE(2);
 
     auto load_x = [&](int tok, int pos, uint32_t (&xf)[LPOS / 2]) {
 #pragma unroll
@@ -397,9 +379,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
         }
     }
     cp_async_wait<0>();
-    TRACE(3);
     __syncthreads();
-    TRACE(4);
 
     // Tiles split between warps: sum the warps' partials in warp order.
     for (int t = warp; t < T; t += kWarps) {
@@ -427,7 +407,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
         }
         emit(t, v);
     }
-    TRACE(5);
 
     if (p.arg_out != nullptr) {
 #pragma unroll
@@ -506,17 +485,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_stream_kernel(const GemvP
 //     x rows sit in shared memory 16 bytes apart modulo 128 (bank-conflict free).
 //     MT = 16 (9..16 tokens): a second MMA per k-step on the same converted
 //     weights for tokens 8..15.
+// Fault bits (AF_FAULT_*) of this device's GEMV kernels, read by af_device_faults.
+__device__ unsigned int g_gemv_faults;
+
 template <bool GROUP, bool F16, int kWarps, int kS, int kMinCtas, bool PAIR, int MT = 1>
 __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(const GemvParams p) {
     constexpr int kThreads = kWarps * 32;
     constexpr int kSlot = 2048;
     constexpr int NQ = MT == 16 ? 8 : 4;   // accumulators per lane
-#ifdef AF_EXP_TRACE
-    __shared__ unsigned s_tl;
-    if (threadIdx.x == 0) s_tl = atomicAdd(&g_trace_launch, 1) / gridDim.x;
-    __syncthreads();
-#endif
-    TRACE(0);
     pdl_launch_dependents();
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char* ring = smem;
@@ -626,7 +602,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     if (threadIdx.x == 32) bulk_prefetch_l2(p.x, (uint32_t)p.M * p.K * 2u);
 
     pdl_wait();
-    TRACE(1);
     // x by one bulk copy on the TMA engine (see above)
     if (threadIdx.x == 0) {
         if (MT == 1) {
@@ -644,7 +619,8 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         s_ep = ldcg_s32(reinterpret_cast<const int*>(p.tp_buf[p.tp_rank] + TpLayout::epoch) + cta) + 1;
     cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
-    mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull);
+    if (!mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull))
+        atomicOr(&g_gemv_faults, (unsigned)AF_FAULT_X_COPY);   // y is not valid: the host sees the fault bit
     if (MT == 1 && p.norm_w != nullptr) {
         // RMSNorm of x in place, in the reference's arithmetic order
         // (src/kernel/rmsnorm.cu:9-67, 128 threads): per-thread strided FMA
@@ -674,7 +650,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
     }
 #pragma unroll 1
     for (int q = p.pre; q < kS; ++q) issue();
-    TRACE(2);
 
     // ---- compute cursor ----
     const unsigned char* my_ring_p = ring + (size_t)warp * kS * kSlot + lane * 16;
@@ -903,7 +878,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         }
     }
     cp_async_wait<0>();
-    TRACE(3);
     __syncthreads();   // every warp is done with the ring
 #pragma unroll
     for (int q = 0; q < NQ / 4; ++q) {
@@ -913,7 +887,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             make_float4(part1[4 * q], part1[4 * q + 1], part1[4 * q + 2], part1[4 * q + 3]);
     }
     __syncthreads();
-    TRACE(4);
 
     // Tiles split between warps: sum the owners' partials in warp order.  The
     // owners come from the warp-start table (no divisions on this serial tail).
@@ -941,7 +914,6 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
         if (owners < 2) continue;   // one owner: emitted from the main loop
         emit(t, v);
     }
-    TRACE(5);
 
     if (p.tp_world > 1 && !p.tp_arg) {
         // Sum this CTA's rows over the ranks, in rank order: each word is
@@ -1152,43 +1124,6 @@ Plan make_plan(int nt, int N, int K, int wk, int sms, bool argmax) {
     return pl;
 }
 
-// AF_M1_VARIANT=0..2 selects the one-token kernel's shape (tuning runs).
-int m1_variant() {
-    static int v = [] {
-        const char* e = getenv("AF_M1_VARIANT");
-        int k = e ? atoi(e) : 0;
-        return (k >= 0 && k <= 6) ? k : 0;
-    }();
-    return v;
-}
-
-// AF_M1_PRE=n: ring slots requested before griddepcontrol.wait (tuning; default all).
-int m1_pre(int ns) {
-    static int v = [] {
-        const char* e = getenv("AF_M1_PRE");
-        return e ? atoi(e) : -1;
-    }();
-    return (v < 0 || v > ns) ? ns : v;
-}
-
-// AF_M1_MT16=0 routes 9..16 tokens through the general kernel (A/B runs).
-bool mt16_enabled() {
-    static bool v = [] {
-        const char* e = getenv("AF_M1_MT16");
-        return !(e && e[0] == '0');
-    }();
-    return v;
-}
-
-// AF_M1_KERNEL=0 routes one-token FP8 GEMVs through the general kernel (for A/B runs).
-bool m1_enabled() {
-    static bool v = [] {
-        const char* e = getenv("AF_M1_KERNEL");
-        return !(e && e[0] == '0');
-    }();
-    return v;
-}
-
 constexpr int kWarpsPerCta = 16;
 constexpr int kRingSlots = 10;   // chunk slots per warp (1 KB each)
 
@@ -1336,7 +1271,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     const size_t gam = (fz != nullptr && fz->norm_w != nullptr) ? round_up((size_t)K * 4, 128) : 0;
     // 2..8 tokens: the one-token kernel with the tokens in the MMA's columns.
     if (M >= 2 && M <= 16 && fz == nullptr && tp == nullptr && arg_out == nullptr && wk != W_F16 &&
-        K % 128 == 0 && aligned(x, 16) && m1_enabled() && (M <= 8 || mt16_enabled())) {
+        K % 128 == 0 && aligned(x, 16)) {
         const size_t stride = (size_t)K + 8;   // halves: token rows 16 B apart modulo 128
         const size_t xs1 = round_up((size_t)M * stride * 2, 128);
         const size_t sc1 = (sc && sc <= 16 * 1024) ? sc : 0;
@@ -1347,7 +1282,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
                 const size_t smem1 = (size_t)8 * o.ns * 2048 + xs1 + scx;
                 if (smem1 > o.cap) continue;
                 prm.xs_stride = (int)stride;
-                prm.pre = m1_pre(o.ns);
+                prm.pre = o.ns;
                 prm.xs_bytes = (int)xs1;
                 prm.sc_bytes = (int)scx;
                 cudaError_t e;
@@ -1362,23 +1297,21 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
     }
     // The decode case -- one token, FP8 weights, whole 128-wide groups -- has
     // its own kernel, sized so that two CTAs (of consecutive GEMVs) share an SM.
-    if (M == 1 && (wk == W_F16 ? K % 64 : K % 128) == 0 && aligned(x, 16) && m1_enabled()) {
-        // (warps, ring slots) options, most in-flight bytes first; two CTAs per SM.
+    if (M == 1 && (wk == W_F16 ? K % 64 : K % 128) == 0 && aligned(x, 16)) {
+        // (warps, ring slots): 8 warps with a 5-slot ring (80 KB, two CTAs per SM),
+        // or 3 slots when the staged x / scales / norm weight need the room.
         struct Cfg { int nw, ns; };
-        const int var = m1_variant();
-        const Cfg cfgs[7][3] = {{{8, 5}, {8, 3}, {8, 3}}, {{16, 3}, {16, 2}, {16, 2}}, {{12, 4}, {12, 2}, {12, 2}}, {{6, 5}, {6, 3}, {6, 3}},
-                                {{8, 12}, {8, 8}, {8, 8}}, {{16, 6}, {16, 4}, {16, 4}}, {{8, 5}, {8, 3}, {8, 3}}};
+        const Cfg cfgs[2] = {{8, 5}, {8, 3}};
         const size_t xs1 = round_up((size_t)K * 2, 128);
         const size_t sc1 = (sc && sc <= (pair ? 32 : 16) * 1024) ? sc : 0;
-        for (const Cfg& cf : cfgs[var]) {
-            const bool deep = cf.nw * cf.ns * 2 > 100;
-            const size_t cap = deep ? kSmemMax - 1024 : (cf.nw <= 6 ? 75 : 113) * 1024;   // 1, 3 or 2 CTAs per SM
+        for (const Cfg& cf : cfgs) {
+            const size_t cap = 113 * 1024;   // two CTAs per SM
             const size_t slots1 = 0;   // the warp partials reuse the ring
             const size_t ring1 = (size_t)cf.nw * cf.ns * 2048;   // >= the 1 KB per warp the partials need
             for (size_t scx : {sc1, (size_t)0}) {
                 if (ring1 + slots1 + xs1 + scx + gam > cap) continue;
                 prm.xs_stride = 0;
-                prm.pre = m1_pre(cf.ns);
+                prm.pre = cf.ns;
                 prm.xs_bytes = (int)xs1;
                 prm.sc_bytes = (int)scx;
                 prm.gam_bytes = (int)gam;
@@ -1389,12 +1322,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
                        : grp ? launch_m1<true, false, NW, NS>(prm, pl, smem1, st) \
                        : f16 ? launch_m1<false, true, NW, NS>(prm, pl, smem1, st) \
                              : launch_m1<false, false, NW, NS>(prm, pl, smem1, st))
-                if (cf.nw == 8 && cf.ns <= 6) e = cf.ns == 6 ? AF_M1(8, 6) : cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
-                else if (cf.nw == 16 && cf.ns <= 3) e = cf.ns == 3 ? AF_M1(16, 3) : AF_M1(16, 2);
-                else if (cf.nw == 12) e = cf.ns == 4 ? AF_M1(12, 4) : AF_M1(12, 2);
-                else if (cf.nw == 6) e = cf.ns == 5 ? AF_M1(6, 5) : AF_M1(6, 3);
-                else if (cf.nw == 8) e = cf.ns == 12 ? AF_M1(8, 12) : AF_M1(8, 8);
-                else e = cf.ns == 6 ? AF_M1(16, 6) : AF_M1(16, 4);
+                e = cf.ns == 5 ? AF_M1(8, 5) : AF_M1(8, 3);
 #undef AF_M1
                 return e == cudaSuccess ? AF_OK : cuda_fail(e, "gemv_fp8_m1_kernel");
             }
@@ -1417,6 +1345,17 @@ int wkind_of(af_scale_kind kind) { return kind == AF_SCALE_GROUP_F16 ? W_FP8_GRO
 
 }  // namespace
 }  // namespace af
+
+unsigned af::gemv_faults(bool clear, cudaError_t* err) {
+    unsigned v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemv_faults, sizeof(v));
+    if (e == cudaSuccess && clear && v != 0) {
+        const unsigned z = 0;
+        e = cudaMemcpyToSymbol(g_gemv_faults, &z, sizeof(z));
+    }
+    *err = e;
+    return v;
+}
 
 using namespace af;
 
@@ -1507,7 +1446,7 @@ extern "C" af_status af_w8a16_gemv_allreduce(const void* x, const void* w, const
     if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return AF_ERR_INVALID;
     if (comm->world == 1)
         return af_w8a16_gemv(x, w, scales, y, 1, N, K, group_size, kind, nullptr, 0, stream);
-    if (K % 128 != 0 || !aligned(x, 16) || !aligned(w, 16) || !m1_enabled()) return AF_ERR_UNSUPPORTED;
+    if (K % 128 != 0 || !aligned(x, 16) || !aligned(w, 16)) return AF_ERR_UNSUPPORTED;
     return run_gemv(wkind_of(kind), static_cast<const __half*>(x), static_cast<const uint8_t*>(w), scales, y, 0, 1,
                     N, K, nullptr, 0, nullptr, 0, static_cast<cudaStream_t>(stream), comm);
 }
@@ -1530,7 +1469,7 @@ extern "C" af_status af_lm_head_gemv_tp(const void* x, const void* w, af_weight_
         return af_lm_head_gemv(x, w, w_dtype, row_scale, logits, V_local, D, d_argmax, mode, workspace,
                                workspace_bytes, stream);
     const int wk = (w_dtype == AF_W_F16) ? W_F16 : W_FP8_ROW;
-    if ((wk == W_F16 ? D % 64 : D % 128) != 0 || !aligned(x, 16) || !aligned(w, 16) || !m1_enabled())
+    if ((wk == W_F16 ? D % 64 : D % 128) != 0 || !aligned(x, 16) || !aligned(w, 16))
         return AF_ERR_UNSUPPORTED;
     // ref-compat: only global ids < 65536 are candidates
     long long lim = V_local;
@@ -1548,7 +1487,7 @@ af_status fused_checks(const void* x, const void* w, const void* scales, const v
     if (kind != AF_SCALE_GROUP_F16 && kind != AF_SCALE_ROW_F32) return AF_ERR_INVALID;
     if (kind == AF_SCALE_GROUP_F16 && group_size != 128) return AF_ERR_INVALID;
     if (K % 128 != 0 || !aligned(y, 2)) return AF_ERR_INVALID;
-    if (!aligned(x, 16) || !aligned(w, 16) || !m1_enabled()) return AF_ERR_UNSUPPORTED;
+    if (!aligned(x, 16) || !aligned(w, 16)) return AF_ERR_UNSUPPORTED;
     return AF_OK;
 }
 }  // namespace

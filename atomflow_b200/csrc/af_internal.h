@@ -17,9 +17,13 @@ int device_sm_count(int* device_out = nullptr);
 // Record a CUDA failure for af_last_cuda_error() and map it to AF_ERR_CUDA.
 af_status cuda_fail(cudaError_t e, const char* where);
 
-// CTAs launched per SM by the streaming kernels (default 1; AF_CTAS_PER_SM
-// overrides it for tuning experiments).
-int ctas_per_sm();
+// CTAs launched per SM by the streaming kernels.
+constexpr int ctas_per_sm() { return 1; }
+
+// Fault bits recorded on the current device by the GEMV (af_gemv.cu) and
+// decode-step (af_decode.cu) kernels; `clear` resets them.  Synchronous.
+unsigned gemv_faults(bool clear, cudaError_t* err);
+unsigned decode_faults(bool clear, cudaError_t* err);
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }

@@ -6,6 +6,7 @@
 #include <cstddef>
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/atomflow_b200.h"
@@ -84,6 +85,13 @@ af_status workspace_for(size_t need, cudaStream_t stream, void** out) {
 
 extern "C" int af_view_last_status(void) { return g_last_status; }
 
+static std::atomic<int> g_argmax_mode{AF_ARGMAX_REF_COMPAT};
+
+extern "C" int af_view_set_argmax_mode(int mode) {
+    if (mode != AF_ARGMAX_TRUE && mode != AF_ARGMAX_REF_COMPAT) return -1;
+    return g_argmax_mode.exchange(mode);
+}
+
 void launch_w8a16_gemv(const View& act_x, const View& weight, const View& scales, View& output,
                        int group_size, cudaStream_t stream) {
     // Same shape source as the reference launcher (qkv_gemm.cu:137-139): N and K
@@ -113,8 +121,8 @@ void launch_w8a16_gemv(const View& act_x, const View& weight, const View& scales
 }
 
 void launch_argmax(const View& logits, int* out_token_id, cudaStream_t stream) {
-    // argmax.cu:93 takes V from the last dim.  This launcher returns the true
-    // argmax; AF_ARGMAX_REF_COMPAT through the C ABI gives the reference's.
+    // argmax.cu:93 takes V from the last dim.  The mode is the reference's
+    // (ids < 65536) unless af_view_set_argmax_mode chose the true argmax.
     if (logits.dtype != DataType::FP32) {
         report(AF_ERR_INVALID, "launch_argmax");
         return;
@@ -125,7 +133,7 @@ void launch_argmax(const View& logits, int* out_token_id, cudaStream_t stream) {
     af_status st = workspace_for(need, stream, &ws);
     if (st == AF_OK)
         st = af_argmax_f32(static_cast<const float*>(logits.data_ptr), V, out_token_id,
-                           AF_ARGMAX_TRUE, ws, need, stream);
+                           static_cast<af_argmax_mode>(g_argmax_mode.load()), ws, need, stream);
     report(st, "launch_argmax");
 }
 

@@ -34,7 +34,7 @@ from .weights_bin import BinFile
 
 NORM_EPS = 1e-5
 ROPE_BASE = 500000.0
-MAX_SEQ_LEN = 2048   # the reference engine's static KV cache length (engine.h:22)
+MAX_SEQ_LEN = 4096   # KV-cache rows: BASELINE config 3 (the reference engine has 2048, engine.h:41)
 
 
 class DecodeEngine:
@@ -145,7 +145,7 @@ class DecodeEngine:
             check(L.af_rmsnorm_w8a16_gemv(p(self.x), p(ly["in_norm"]), NORM_EPS, p(wq), p(sq), p(self.qkv),
                                           self.QD + 2 * self.KVD, self.D, 128, 0, None, st), "rmsnorm_gemv")
             check(L.af_decode_rope_attention(p(self.qkv), p(self.cos), p(self.sin), p(self.d_pos), p(ly["k_cache"]),
-                                             p(ly["v_cache"]), p(self.attn), self.NH, self.NKV, self.HD,
+                                             p(ly["v_cache"]), p(self.attn), self.NH, self.NKV, self.HD, self.max_seq,
                                              p(self.attn_ws), self.attn_ws.numel(), st), "rope_attention")
             wo, so = ly["o"]
             check(L.af_w8a16_gemv_residual(p(self.attn), p(wo), p(so), p(self.x), self.D, self.QD, 128, 0, None, st),

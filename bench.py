@@ -539,7 +539,8 @@ def run_decode(args, device, local):
                                      "kind": "reference", "sample": "the reference's AtomFlowEngine (CUDA, compiled "
                                      "from its sources), graph of forward_pass at position 1024, on this GPU"}})
         print(json.dumps(out))
-        os._exit(0)
+        R.afref_engine_destroy(h)
+        return 0
     from atomflow_b200.decode import DecodeEngine
     eng = DecodeEngine(path)
     rng = np.random.default_rng(0)
@@ -606,7 +607,7 @@ def run_decode(args, device, local):
                         "path": "DecodeEngine over the C ABI: token H2D from pinned memory, the step, next token D2H "
                                 "to pinned memory, one CUDA graph per step"}})
     print(json.dumps(out))
-    os._exit(0)
+    return 0
 
 
 def main():
@@ -789,8 +790,10 @@ def main():
                                    if lm else "fused into the GEMV over NVLink peer memory") if comm is not None
                                   else "NCCL all_reduce after the GEMV")
 
+    g = ge = None          # graphs (and any NCCL work they captured) go before the process group
+    torch.cuda.synchronize()
     if rank != 0:
-        finish(dist_on)
+        return finish(dist_on)
 
     peak, peak_kind = measured_peaks()
     per_rank_gbs = step_bytes / (ms_step / 1e3) / 1e9
@@ -829,20 +832,20 @@ def main():
                                          "w8a16_gemv_kernel, compiled from its sources), run on this GPU"}
         out["reference_kernel_launches"] = launches * (items[0]["x"].shape[0] if wl.startswith("gemv:") else 1)
     print(json.dumps(out))
-    finish(dist_on)
+    return finish(dist_on)
 
 
 def finish(dist_on):
-    """Leave without tearing NCCL down: graphs that captured NCCL collectives are
-    still alive, and destroying the communicator under them can block.  All
-    ranks meet at a barrier first, so no rank exits with work in flight."""
+    """Normal exit: all ranks meet at a barrier (no rank leaves with work in
+    flight), then the process group is destroyed and main returns."""
     torch.cuda.synchronize()
     if dist_on:
         torch.distributed.barrier()
         torch.cuda.synchronize()
+        torch.distributed.destroy_process_group()
     sys.stdout.flush()
     sys.stderr.flush()
-    os._exit(0)
+    return 0
 
 
 def traffic_from_profiles(workload, launches_per_step):

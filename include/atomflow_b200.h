@@ -54,7 +54,17 @@ typedef enum af_argmax_mode {
     AF_ARGMAX_REF_COMPAT = 1  /* the reference's result: only ids < 65536 are candidates */
 } af_argmax_mode;
 
+/* Fault bits a kernel records on its device instead of faulting the GPU. */
+typedef enum af_fault_bits {
+    AF_FAULT_X_COPY = 1,      /* a GEMV's bounded wait for its x copy ran out (that y is invalid) */
+    AF_FAULT_POSITION = 2     /* a decode kernel read a position outside [0, max_seq) and skipped its work */
+} af_fault_bits;
+
 const char* af_status_string(af_status s);
+/* The AF_FAULT_* bits recorded on the current device since the last clear (0:
+ * none); clear != 0 resets them.  Synchronous (reads device memory), so call it
+ * outside stream capture, e.g. after a run of graph replays. */
+af_status af_device_faults(unsigned* out, int clear);
 /* Error string of the last CUDA failure seen by this library on this thread. */
 const char* af_last_cuda_error(void);
 int af_version(void);
@@ -193,21 +203,24 @@ af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const v
  *                        it zeroed.  (tiled_attention.cu gqa_cached_attention_kernel)
  *   af_rmsnorm           the reference's rms_norm arithmetic, one vector
  *   af_decode_advance    *d_pos += by (the step's last launch)
+ * max_seq is the caches' and tables' row count: a kernel that reads *d_pos
+ * outside [0, max_seq) writes and reads nothing, leaves its outputs as they
+ * were and sets AF_FAULT_POSITION (af_device_faults).
  */
 af_status af_embed_lookup(const float* table, const int* d_token, void* x, int D, void* stream);
 af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq, int head_dim, float base);
 af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos, void* k_cache,
-                           void* v_cache, int n_heads, int n_kv_heads, int head_dim, void* stream);
+                           void* v_cache, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* stream);
 size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads);
 af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos, void* out,
-                              int n_heads, int n_kv_heads, int head_dim, void* workspace, size_t workspace_bytes,
-                              void* stream);
+                              int n_heads, int n_kv_heads, int head_dim, int max_seq, void* workspace,
+                              size_t workspace_bytes, void* stream);
 /* RoPE + KV-cache write + attention in one launch: q, k, v read from the raw qkv vector; the same
  * results, bit for bit, as af_rope_kv_write followed by af_decode_attention (qkv itself is left
  * unrotated). */
 af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                    void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
-                                   int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+                                   int head_dim, int max_seq, void* workspace, size_t workspace_bytes, void* stream);
 af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream);
 af_status af_decode_advance(int* d_pos, int by, void* stream);
 

@@ -53,7 +53,12 @@ struct View {
 void launch_w8a16_gemv(const View& act_x, const View& weight, const View& scales,
                        View& output, int group_size, cudaStream_t stream);
 
-/* include/ops/kernel.h:155-159 -- greedy argmax of FP32 logits [.., V]. */
+/* include/ops/kernel.h:155-159 -- greedy argmax of FP32 logits [.., V].
+ * By default it gives the reference launcher's result: only ids below 65,536
+ * are candidates (src/kernel/argmax.cu:72-73, 115-117 read 256 of the 501
+ * per-block partials), so an engine linked against this library emits the same
+ * tokens as the unmodified build.  af_view_set_argmax_mode(AF_ARGMAX_TRUE = 0)
+ * switches this process to the true argmax over all V ids. */
 void launch_argmax(const View& logits, int* out_token_id, cudaStream_t stream);
 
 /* include/ops/kernel.h:53-59 -- FP8 weight x FP16 activation linear layer
@@ -63,5 +68,9 @@ void launch_linear_gemm(const View& input, const View& weight, View& output,
                         cublasHandle_t handle, cudaStream_t stream);
 
 extern "C" int af_view_last_status(void);
+/* Mode of launch_argmax for the whole process: 1 (AF_ARGMAX_REF_COMPAT, the
+ * default) or 0 (AF_ARGMAX_TRUE).  Returns the previous mode, or -1 for an
+ * unknown mode (nothing changes). */
+extern "C" int af_view_set_argmax_mode(int mode);
 
 #endif /* ATOMFLOW_VIEW_OPS_H */

@@ -19,11 +19,11 @@ _ref = None
 
 
 def build(ref_sources=None):
-    """Compile liboracle.so; also _ref/libafref.so when the reference sources exist."""
+    """Compile liboracle.so; also the reference's own kernels and engine into
+    _ref/ when `ref_sources` names a reference checkout."""
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
-    src = Path(ref_sources or "/root/reference")
-    if (src / "src" / "kernel" / "qkv_gemm.cu").exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={src}"], check=True)
+    if ref_sources is not None and (Path(ref_sources) / "src" / "kernel" / "qkv_gemm.cu").exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref_sources}"], check=True)
 
 
 def _p(a):

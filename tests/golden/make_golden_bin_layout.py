@@ -2,7 +2,7 @@
 REFERENCE's own weight loader (include/memory/weight_loader.h) arrives at when
 it walks a tiny random-init file in src/core/engine.cu:103-147's order.
 
-Needs the reference checkout (REF, default /root/reference) and g++; run it
+Needs the reference checkout (environment variable REF) and g++; run it
 where both exist.  The walker below is this project's code: it includes the
 reference header and calls its WeightLoader::next<T>() with engine.cu's sizes.
 """
@@ -17,7 +17,7 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 from atomflow_b200.weights_bin import ModelShape, write_synthetic_bin  # noqa: E402
 
-REF = os.environ.get("REF", "/root/reference")
+REF = os.environ.get("REF") or sys.exit("set REF=<reference checkout>")
 SHAPE = ModelShape(dim=256, ffn=512, n_layers=2, n_heads=4, n_kv_heads=2, vocab=1000, max_seq_len=64)
 
 WALKER = r'''

@@ -12,7 +12,7 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+REF = Path(sys.argv[1]) if len(sys.argv) > 1 else sys.exit("usage: make_golden_quant.py <reference checkout>")
 sys.path.insert(0, str(REF / "tools"))
 from quantize_weights import quantize_fp8_gs128  # noqa: E402
 

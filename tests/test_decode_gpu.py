@@ -75,7 +75,7 @@ def test_rope_kv_write_matches_reference():
         vc_a, kc_b, vc_b = kc_a.clone(), kc_a.clone(), kc_a.clone()
         dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
         assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kc_a.data_ptr(),
-                                  vc_a.data_ptr(), NH, NKV, HD, st()) == 0
+                                  vc_a.data_ptr(), NH, NKV, HD, MAXSEQ, st()) == 0
         assert ref().afref_rope_kv(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), kc_b.data_ptr(), vc_b.data_ptr(),
                                    pos, NH, NKV, HD, st()) == 0
         torch.cuda.synchronize()
@@ -137,7 +137,7 @@ def test_decode_attention_parity():
         for _ in range(2):   # two calls in a row: the workspace is left zeroed
             o = torch.zeros(NH * HD, dtype=torch.float16, device="cuda")
             assert L.af_decode_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), dpos.data_ptr(), o.data_ptr(),
-                                         NH, NKV, HD, ws.data_ptr(), ws.numel(), st()) == 0
+                                         NH, NKV, HD, MAXSEQ, ws.data_ptr(), ws.numel(), st()) == 0
             outs.append(o)
         o_ref = torch.zeros(NH * HD, dtype=torch.float16, device="cuda")
         assert ref().afref_cached_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), o_ref.data_ptr(), pos + 1, HD,
@@ -170,18 +170,57 @@ def test_fused_rope_attention_equals_the_two_kernels():
         ob = torch.zeros_like(oa)
         a = qkv.clone()
         assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), ka.data_ptr(),
-                                  va.data_ptr(), NH, NKV, HD, st()) == 0
+                                  va.data_ptr(), NH, NKV, HD, MAXSEQ, st()) == 0
         assert L.af_decode_attention(a.data_ptr(), ka.data_ptr(), va.data_ptr(), dpos.data_ptr(), oa.data_ptr(), NH,
-                                     NKV, HD, ws_a.data_ptr(), ws_a.numel(), st()) == 0
+                                     NKV, HD, MAXSEQ, ws_a.data_ptr(), ws_a.numel(), st()) == 0
         b = qkv.clone()
         assert L.af_decode_rope_attention(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kb.data_ptr(),
-                                          vb.data_ptr(), ob.data_ptr(), NH, NKV, HD, ws_b.data_ptr(), ws_b.numel(),
+                                          vb.data_ptr(), ob.data_ptr(), NH, NKV, HD, MAXSEQ, ws_b.data_ptr(), ws_b.numel(),
                                           st()) == 0
         torch.cuda.synchronize()
         assert torch.equal(oa.view(torch.int16), ob.view(torch.int16)), pos
         assert torch.equal(ka.view(torch.int16), kb.view(torch.int16)), pos
         assert torch.equal(va.view(torch.int16), vb.view(torch.int16)), pos
         assert torch.equal(b, qkv)   # the fused kernel leaves qkv unrotated
+
+
+def test_position_outside_the_cache_is_skipped_and_flagged():
+    """A device-side position at or past max_seq (a replayed step that ran past
+    the cache) must write nothing and set AF_FAULT_POSITION, not write out of
+    bounds."""
+    L = lib()
+    cos, sin = _tables()
+    qd, kvd = NH * HD, NKV * HD
+    flt = ctypes.c_uint(0)
+    assert L.af_device_faults(ctypes.byref(flt), 1) == 0
+    ws = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV), dtype=torch.uint8, device="cuda")
+    qkv = torch.randn(qd + 2 * kvd, device="cuda").half()
+    small = 64   # caches with 64 rows; the buffers run on past them, so a stray write would show
+    kc = torch.zeros(2 * small, kvd, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    o = torch.full((qd,), 7.0, dtype=torch.float16, device="cuda")
+    for pos in (small, small + 5, -1):
+        dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        assert L.af_decode_rope_attention(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(),
+                                          kc.data_ptr(), vc.data_ptr(), o.data_ptr(), NH, NKV, HD, small,
+                                          ws.data_ptr(), ws.numel(), st()) == 0
+        assert L.af_rope_kv_write(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), kc.data_ptr(),
+                                  vc.data_ptr(), NH, NKV, HD, small, st()) == 0
+        torch.cuda.synchronize()
+        assert not kc.any() and not vc.any() and bool((o == 7.0).all()), pos
+        assert L.af_device_faults(ctypes.byref(flt), 1) == 0
+        assert flt.value & 2, pos
+    assert L.af_device_faults(ctypes.byref(flt), 0) == 0 and flt.value == 0
+    # the workspace is still usable: an in-range call afterwards matches a fresh workspace
+    dpos = torch.tensor([small - 1], dtype=torch.int32, device="cuda")
+    outs = []
+    for w in (ws, torch.zeros_like(ws)):
+        oo = torch.zeros(qd, dtype=torch.float16, device="cuda")
+        assert L.af_decode_attention(qkv.data_ptr(), kc.data_ptr(), vc.data_ptr(), dpos.data_ptr(), oo.data_ptr(),
+                                     NH, NKV, HD, small, w.data_ptr(), w.numel(), st()) == 0
+        outs.append(oo)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_decode_engine_tokens_match_reference(tmp_path):

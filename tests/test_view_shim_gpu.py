@@ -46,9 +46,25 @@ def test_launch_argmax_and_linear_gemm_view():
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
     lv = make_view(vd.data_ptr(), DataType.FP32, [1, V])
     st = torch.cuda.current_stream().cuda_stream
+    # default: the reference launcher's result, ids < 65536 only (argmax.cu:72-73, 115-117)
+    want_ref = int(np.argmax(v[0, :65536]))
     L.launch_argmax(ctypes.byref(lv), ctypes.c_void_p(out.data_ptr()), st)
     torch.cuda.synchronize()
-    assert L.af_view_last_status() == 0 and int(out.item()) == 99999
+    assert L.af_view_last_status() == 0 and int(out.item()) == want_ref
+    R = oracle.ref()
+    if R is not None:   # the reference's own launch_argmax on the same logits
+        ro = torch.zeros(1, dtype=torch.int32, device="cuda")
+        assert R.afref_argmax(vd.data_ptr(), V, ro.data_ptr(), st) == 0
+        torch.cuda.synchronize()
+        assert int(ro.item()) == want_ref
+    assert L.af_view_set_argmax_mode(0) == 1
+    try:
+        L.launch_argmax(ctypes.byref(lv), ctypes.c_void_p(out.data_ptr()), st)
+        torch.cuda.synchronize()
+        assert L.af_view_last_status() == 0 and int(out.item()) == 99999
+    finally:
+        assert L.af_view_set_argmax_mode(1) == 0
+    assert L.af_view_set_argmax_mode(7) == -1
     M, N, K = 4, 256, 512
     x, q, _ = make_gemv_case(5, M, N, K, kind="none")
     xd = torch.from_numpy(x.view(np.int16)).cuda()

@@ -141,6 +141,23 @@ def write_synthetic_bin(path, shape: ModelShape = ModelShape(), seed: int = 0, d
     return total
 
 
+def synthetic_model_file(shape: ModelShape = ModelShape(), seed: int = 0, directory=None) -> Path:
+    """A random-init model file of `shape`, written once (values drawn on the
+    GPU) under `directory` (default: the system temp dir, or $AF_MODEL_DIR)
+    and reused by later calls with the same shape and seed."""
+    import os
+    import tempfile
+    d = Path(directory or os.environ.get("AF_MODEL_DIR") or tempfile.gettempdir())
+    tag = "-".join(str(v) for v in (shape.dim, shape.ffn, shape.n_layers, shape.n_heads, shape.n_kv_heads,
+                                    shape.vocab, shape.max_seq_len))
+    path = d / f"af_synthetic_{tag}_seed{seed}.bin"
+    if not path.exists() or path.stat().st_size != block_plan(shape)[1]:
+        tmp = path.with_suffix(f".part{os.getpid()}")
+        write_synthetic_bin(tmp, shape, seed=seed, device="cuda")
+        os.replace(tmp, path)
+    return path
+
+
 class BinFile:
     """Read-only view of a `.bin` model file (mmap), block by block."""
 

@@ -485,18 +485,14 @@ def cpu_baseline(items, budget_s=10.0):
 # -------------------------------------------------------------------- main
 
 DECODE_POS = 1024
+TOKEN_CHECK_STEPS = 64
 
 
 def decode_model_path():
     """BASELINE config 3's random-init model in the reference's .bin format,
     written once per box (generated on the GPU) and shared by both arms."""
-    from atomflow_b200.weights_bin import ModelShape, write_synthetic_bin
-    path = Path(os.environ.get("AF_DECODE_BIN", "/tmp/af_decode_llama3.2-3b_seed0.bin"))
-    if not path.exists():
-        tmp = path.with_suffix(".part")
-        write_synthetic_bin(tmp, ModelShape(), seed=0, device="cuda")
-        tmp.rename(path)
-    return path
+    from atomflow_b200.weights_bin import ModelShape, synthetic_model_file
+    return synthetic_model_file(ModelShape(), seed=0)
 
 
 def run_decode(args, device, local):
@@ -556,6 +552,9 @@ def run_decode(args, device, local):
         eng.current_pos = DECODE_POS
     eng.stream.synchronize()
     assert eng.current_pos == DECODE_POS
+    first_token = eng.get_output_token()  # the prefill's last output: the first greedy step's input
+    if DECODE_POS + max(args.warmup, args.steps + 3, TOKEN_CHECK_STEPS) >= eng.max_seq:
+        raise SystemExit(f"--steps/--warmup would run past the {eng.max_seq}-row KV cache")
     for _ in range(args.warmup):          # greedy warm-up steps, then rewind
         eng.replay(g)
     eng.current_pos = DECODE_POS
@@ -592,6 +591,30 @@ def run_decode(args, device, local):
     eng.stream.synchronize()
     e2e_ms = ev0.elapsed_time(ev1) / args.steps
     sampler.stop()
+    # greedy tokens from position DECODE_POS, checked against the reference engine's
+    eng.current_pos = DECODE_POS
+    eng.inject_token(first_token)
+    ours_toks = []
+    for _ in range(TOKEN_CHECK_STEPS):
+        eng.replay(g)
+        ours_toks.append(eng.get_output_token())
+    tokens = {"greedy_steps": TOKEN_CHECK_STEPS, "from_position": DECODE_POS, "ours": ours_toks}
+    import oracle
+    R = oracle.ref_engine() if not args.no_token_check and config["kv_cache"].startswith("prefilled") else None
+    if R is not None:
+        h = R.afref_engine_create(str(path).encode())
+        tok = None
+        ref_toks = []
+        for pos in range(DECODE_POS + TOKEN_CHECK_STEPS):
+            tok = R.afref_engine_step(h, int(prompt[pos]) if pos < DECODE_POS else tok, pos)
+            if pos >= DECODE_POS:
+                ref_toks.append(tok)
+        R.afref_engine_destroy(h)
+        div = [i for i, (a, b) in enumerate(zip(ours_toks, ref_toks)) if a != b]
+        tokens.update({"reference": ref_toks, "match_reference": not div,
+                       "first_divergence": (DECODE_POS + div[0]) if div else None})
+    else:
+        tokens["match_reference"] = None
     step_bytes = eng.weight_bytes() + eng.kv_bytes(DECODE_POS + args.steps // 2)
     achieved = step_bytes / (ms / 1e3) / 1e9
     out.update({"value": round(1000.0 / ms, 2), "ms_per_step": round(ms, 5), "clocks": clocks,
@@ -601,7 +624,7 @@ def run_decode(args, device, local):
                              "traffic": None, "kernel": "whole step (GEMV kernels carry 94% of the bytes)",
                              "per_launch": f"{step_bytes / 1e9:.3f} GB per step (weights, scales, norms, lm_head, "
                                            f"embedding row, KV cache) over {ms * 1e3:.1f} us"},
-                "gpu_launches": eng.launches_per_step * args.steps,
+                "gpu_launches": eng.launches_per_step * args.steps, "tokens": tokens,
                 "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 5),
                         "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                         "path": "DecodeEngine over the C ABI: token H2D from pinned memory, the step, next token D2H "
@@ -619,6 +642,8 @@ def main():
     ap.add_argument("--workload", default="layerset")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-token-check", action="store_true",
+                    help="decode: skip comparing 64 greedy tokens with the reference engine")
     ap.add_argument("--layers", type=int, default=NLAYERS,
                     help="layers of the layerset / layerchain workloads (default 28; fewer only for profiling)")
     ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",

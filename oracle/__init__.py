@@ -57,14 +57,17 @@ def cpu():
     return _cpu
 
 
-_ref_engine = None
+_ref_engine = {}
 
 
-def ref_engine():
-    """The reference's decode engine (GPU), or None if _ref/libafref_engine.so is absent."""
-    global _ref_engine
-    if _ref_engine is None:
-        path = HERE / "_ref" / "libafref_engine.so"
+def ref_engine(shim=False):
+    """The reference's decode engine (GPU), or None if its library is absent.
+    shim=True: the same unmodified engine.cu linked against this library's View
+    launchers in place of the reference's GEMV and argmax
+    (_ref/libafref_engine_shim.so)."""
+    name = "libafref_engine_shim.so" if shim else "libafref_engine.so"
+    if name not in _ref_engine:
+        path = HERE / "_ref" / name
         if not path.exists():
             return None
         L = ctypes.CDLL(str(path))
@@ -77,8 +80,10 @@ def ref_engine():
         L.afref_engine_step.argtypes = [vp, i, i]
         L.afref_engine_tpot_ms.restype = ctypes.c_float
         L.afref_engine_tpot_ms.argtypes = [vp, i, i, i]
-        _ref_engine = L
-    return _ref_engine
+        L.afref_engine_logits.restype = vp
+        L.afref_engine_logits.argtypes = [vp, ctypes.POINTER(ctypes.c_int)]
+        _ref_engine[name] = L
+    return _ref_engine[name]
 
 
 def ref():

@@ -2,9 +2,17 @@
 // (AtomFlowEngine, src/core/engine.cu), for the decode-step parity test and
 // bench.py's reference arm.  TEST INFRASTRUCTURE ONLY.  Linked by
 // oracle/Makefile with the reference's unmodified engine and kernel sources.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
+#include <string>
+#include <vector>
+
+// The logits View is a private member; the checker reads it (for the top-2
+// margin of a divergent step) without changing the engine's code.
+#define private public
 #include "core/engine.h"
+#undef private
 
 extern "C" void* afref_engine_create(const char* path) {
     AtomFlowEngine* e = new AtomFlowEngine();
@@ -21,6 +29,13 @@ extern "C" int afref_engine_step(void* h, int token, int pos) {
     e->inject_token(token);
     e->forward_pass();
     return e->get_output_token();
+}
+
+// Device pointer of the engine's FP32 logits [V] (ActBuffers::logits) and V.
+extern "C" const void* afref_engine_logits(void* h, int* vocab) {
+    AtomFlowEngine* e = static_cast<AtomFlowEngine*>(h);
+    if (vocab) *vocab = e->V;
+    return e->act_.logits.data_ptr;
 }
 
 // TPOT as main.cu measures it (main.cu:92-150): forward_pass at a fixed

@@ -1,0 +1,114 @@
+"""BASELINE config 3 at its real shape: a Llama-3.2-3B-shaped random-init model
+(28 layers, hidden 3072, GQA 24/8, FFN 8192, vocab 128256) in the reference's
+`.bin` format, KV cache filled by 1024 teacher-forced steps (seeded random
+token ids), then 64 greedy steps from position 1024, in three engines:
+
+  (a) the reference's AtomFlowEngine, unmodified (oracle/_ref/libafref_engine.so);
+  (b) the same unmodified engine.cu linked against this library, whose View
+      launchers replace the reference's launch_w8a16_gemv and launch_argmax
+      (oracle/_ref/libafref_engine_shim.so -- the drop-in as a user gets it);
+  (c) this library's DecodeEngine (fused projections, split-KV attention).
+
+The 64 greedy tokens must be identical in all three.  The 1024 teacher-forced
+argmaxes must agree wherever the reference's top-2 logit margin is not within
+rounding (an argmax whose two best logits are closer than the FP16/FP32
+rounding of a 28-layer forward pass may go either way); the count of such
+near-ties is reported.  The argmax is the reference's (ids < 65536) in all
+three, as the unmodified engine computes it (src/kernel/argmax.cu:72-73).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+PREFILL, GREEDY = 1024, 64
+NEAR_TIE = 2e-2      # logit units (logits have std ~1 on this model); differences of rounding stay far below
+_cudart = None
+
+
+def _d2h_f32(ptr, n):
+    global _cudart
+    if _cudart is None:
+        _cudart = ctypes.CDLL("libcudart.so.12")
+    out = np.empty(n, np.float32)
+    assert _cudart.cudaMemcpy(out.ctypes.data_as(ctypes.c_void_p), ctypes.c_void_p(ptr), ctypes.c_size_t(n * 4),
+                              2) == 0
+    return out
+
+
+def _margin(logits):
+    top = np.partition(logits[:65536], -2)[-2:]
+    return float(top[1] - top[0])
+
+
+def _run_reference(R, path, prompt):
+    h = R.afref_engine_create(str(path).encode())
+    try:
+        V = ctypes.c_int(0)
+        lp = R.afref_engine_logits(h, ctypes.byref(V))
+        toks, margins = [], []
+        tok = None
+        for pos in range(PREFILL + GREEDY):
+            tok = R.afref_engine_step(h, int(prompt[pos]) if pos < PREFILL else tok, pos)
+            toks.append(tok)
+            margins.append(_margin(_d2h_f32(lp, V.value)))
+        return np.array(toks), np.array(margins)
+    finally:
+        R.afref_engine_destroy(h)
+
+
+def _run_ours(path, prompt):
+    from atomflow_b200.decode import DecodeEngine
+    eng = DecodeEngine(path)
+    g = eng.capture(advance=True)
+    eng.current_pos = 0
+    toks = []
+    for pos in range(PREFILL + GREEDY):
+        if pos < PREFILL:
+            eng.inject_token(int(prompt[pos]))
+        eng.replay(g)          # greedy: the step leaves its token in the device int it reads next
+        toks.append(eng.get_output_token())
+    assert eng.current_pos == PREFILL + GREEDY
+    del g, eng
+    torch.cuda.empty_cache()
+    return np.array(toks)
+
+
+def test_config3_tokens_reference_dropin_and_ours():
+    R, RS = oracle.ref_engine(), oracle.ref_engine(shim=True)
+    if R is None or RS is None:
+        pytest.skip("oracle/_ref engine libraries not built")
+    from atomflow_b200 import lib
+    from atomflow_b200.weights_bin import ModelShape, synthetic_model_file
+    L = lib()
+    path = synthetic_model_file(ModelShape(), seed=0)
+    prompt = np.random.default_rng(0).integers(0, 65536, PREFILL)
+
+    ref_toks, ref_margin = _run_reference(R, path, prompt)
+    assert L.af_view_set_argmax_mode(1) >= 0          # the drop-in's default: the reference's argmax
+    shim_toks, _ = _run_reference(RS, path, prompt)
+    assert L.af_view_last_status() == 0
+    ours_toks = _run_ours(path, prompt)
+    flt = ctypes.c_uint(0)
+    assert L.af_device_faults(ctypes.byref(flt), 1) == 0 and flt.value == 0
+
+    report = []
+    for name, toks in (("drop-in", shim_toks), ("ours", ours_toks)):
+        tf = toks[:PREFILL] != ref_toks[:PREFILL]
+        bad = tf & (ref_margin[:PREFILL] >= NEAR_TIE)
+        report.append(f"{name}: teacher-forced argmax differs at {int(tf.sum())} of {PREFILL} positions "
+                      f"(top-2 margins there {np.round(ref_margin[:PREFILL][tf], 4).tolist()}), "
+                      f"{int(bad.sum())} beyond the near-tie bound")
+        gr = np.nonzero(toks[PREFILL:] != ref_toks[PREFILL:])[0]
+        if gr.size:
+            i = PREFILL + int(gr[0])
+            report.append(f"{name}: greedy tokens diverge at position {i} (ours {toks[i]}, reference "
+                          f"{ref_toks[i]}, reference top-2 margin {ref_margin[i]:.5f})")
+        assert not bad.any(), "\n".join(report)
+        assert gr.size == 0, "\n".join(report)
+    print("\n".join(report))

@@ -44,6 +44,22 @@ class AtomflowError(RuntimeError):
         super().__init__(msg)
 
 
+class ChainOp(ctypes.Structure):
+    """af_chain_op (include/atomflow_b200.h)."""
+    _fields_ = [("kind", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int), ("wait_prev", ctypes.c_int),
+                ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+                ("w2", ctypes.c_void_p), ("scales2", ctypes.c_void_p), ("norm_w", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("y", ctypes.c_void_p), ("xn_out", ctypes.c_void_p),
+                ("aux", ctypes.c_void_p)]
+
+
+class OpKind(enum.IntEnum):
+    GEMV = 0
+    GEMV_RESIDUAL = 1
+    RMSNORM_GEMV = 2
+    RMSNORM_SWIGLU = 3
+
+
 # Every symbol include/atomflow_b200.h and include/atomflow_view_ops.h declare,
 # with its ctypes signature (restype, argtypes).
 _vp, _sz, _i, _fp = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p
@@ -83,6 +99,8 @@ C_SYMBOLS = {
     "af_device_faults": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
     "af_rmsnorm": (_i, [_vp, _vp, ctypes.c_float, _vp, _i, _vp]),
     "af_decode_advance": (_i, [_vp, _i, _vp]),
+    "af_chain_workspace_bytes": (_sz, [_i]),
+    "af_gemv_chain": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
     "af_view_last_status": (_i, []),
     "af_view_set_argmax_mode": (_i, [_i]),
 }

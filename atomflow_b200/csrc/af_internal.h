@@ -24,9 +24,21 @@ constexpr int ctas_per_sm() { return 1; }
 // decode-step (af_decode.cu) kernels; `clear` resets them.  Synchronous.
 unsigned gemv_faults(bool clear, cudaError_t* err);
 unsigned decode_faults(bool clear, cudaError_t* err);
+unsigned chain_faults(bool clear, cudaError_t* err);
+
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// The persistent projection-chain kernel (af_chain.cu).  `single`: a one-op
+// call (shallower ring, two CTAs per SM, programmatic dependent launch).
+constexpr int kChainMaxK = 16384;
+af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_t ws_bytes, cudaStream_t st,
+                       bool single);
+inline bool chain_ok(const void* x, const void* w, const void* s, int K) {
+    return K > 0 && K % 128 == 0 && K <= kChainMaxK && x != nullptr && w != nullptr && s != nullptr &&
+           aligned(x, 16) && aligned(w, 16) && aligned(s, 2);
+}
 
 // Launch `kernel` with programmatic stream serialization, so it may begin
 // while the previous kernel of the stream drains; the kernel itself calls

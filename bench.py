@@ -201,10 +201,35 @@ class OursChain:
     N > 1 the row-split O/down are af_w8a16_gemv_allreduce_residual."""
     launches_per_layer = 4
 
-    def __init__(self, bufs):
+    def __init__(self, bufs, as_chain=False):
         self.L = af_lib()
         self.b = bufs
         self.comm = None
+        if as_chain:
+            from atomflow_b200._lib import ChainOp
+            self.ChainOp = ChainOp
+            self.launch_all = self._launch_all
+            self.ws = torch.zeros(self.L.af_chain_workspace_bytes(4 * NLAYERS), dtype=torch.uint8,
+                                  device=bufs["x"].device)
+
+    def _launch_all(self, stream, layers):
+        """All layers' 4 fused projections as ONE persistent launch (af_gemv_chain)."""
+        b, C = self.b, self.ChainOp
+        p = lambda t: t.data_ptr()  # noqa: E731
+        ops = []
+        for ly in layers:
+            q, o, ga, up, dn = (ly[k] for k in ("qkv", "o", "gate", "up", "down"))
+            ops += [C(kind=2, N=q["N"], K=q["K"], wait_prev=1, x=p(b["x"]), w=p(q["q"]), scales=p(q["s"]),
+                      norm_w=p(ly["g_attn"]), eps=NORM_EPS, y=p(b["qkv"])),
+                    C(kind=1, N=o["N"], K=o["K"], wait_prev=1, x=p(b["qkv"]), w=p(o["q"]), scales=p(o["s"]),
+                      y=p(b["x"])),
+                    C(kind=3, N=ga["N"], K=ga["K"], wait_prev=1, x=p(b["x"]), w=p(ga["q"]), scales=p(ga["s"]),
+                      w2=p(up["q"]), scales2=p(up["s"]), norm_w=p(ly["g_mlp"]), eps=NORM_EPS, y=p(b["h"])),
+                    C(kind=1, N=dn["N"], K=dn["K"], wait_prev=1, x=p(b["h"]), w=p(dn["q"]), scales=p(dn["s"]),
+                      y=p(b["x"]))]
+        arr = (C * len(ops))(*ops)
+        self._check(self.L.af_gemv_chain(arr, len(ops), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream),
+                    "af_gemv_chain")
 
     def _check(self, rc, what):
         if rc != 0:
@@ -337,6 +362,34 @@ class OursGemv:
             raise RuntimeError(f"af_w8a16_gemv: {self.L.af_status_string(rc).decode()}")
 
 
+class OursChainSet:
+    """The layer set as ONE persistent launch (af_gemv_chain): every GEMV of the
+    step in order, each waiting for the previous one to finish on every CTA --
+    the same ordering the reference's 140 dependent launches have -- while the
+    next GEMV's weights stream in."""
+    launches_per_item = 1 / 140
+
+    def __init__(self, items, device, wait=True):
+        from atomflow_b200._lib import ChainOp
+        self.L = af_lib()
+        self.wait = wait
+        self.ChainOp = ChainOp
+        self.ws = torch.zeros(self.L.af_chain_workspace_bytes(len(items)), dtype=torch.uint8, device=device)
+
+    def ops(self, items, xptrs=None, yptrs=None):
+        return (self.ChainOp * len(items))(*[
+            self.ChainOp(kind=0, N=it["N"], K=it["K"], wait_prev=int(self.wait and i > 0),
+                         x=xptrs[i] if xptrs else it["x"].data_ptr(), w=it["q"].data_ptr(), scales=it["s"].data_ptr(),
+                         y=yptrs[i] if yptrs else it["y"].data_ptr())
+            for i, it in enumerate(items)])
+
+    def launch_all(self, stream, items, xptrs=None, yptrs=None):
+        ops = self.ops(items, xptrs, yptrs)
+        rc = self.L.af_gemv_chain(ops, len(items), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"af_gemv_chain: {self.L.af_status_string(rc).decode()}")
+
+
 class RefGemv:
     def __init__(self, items, device):
         sys.path.insert(0, str(ROOT))
@@ -404,27 +457,25 @@ class RefLmHead:
 
 
 def capture_step(arm, items, stream, allreduce=None, pre=None, post=None):
+    def step():
+        if pre:
+            pre()
+        if hasattr(arm, "launch_all"):
+            arm.launch_all(stream, items)
+        else:
+            for it in items:
+                arm.launch(stream, it)
+                if allreduce is not None and it["split"] == "row":
+                    allreduce(it["y"])
+        if post:
+            post()
+
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
-        # one eager pass (sets kernel attributes, NCCL warm-up) before capture
-        if pre:
-            pre()
-        for it in items:
-            arm.launch(stream, it)
-            if allreduce is not None and it["split"] == "row":
-                allreduce(it["y"])
-        if post:
-            post()
+        step()     # one eager pass (sets kernel attributes, NCCL warm-up) before capture
     stream.synchronize()
     with torch.cuda.graph(g, stream=stream):
-        if pre:
-            pre()
-        for it in items:
-            arm.launch(stream, it)
-            if allreduce is not None and it["split"] == "row":
-                allreduce(it["y"])
-        if post:
-            post()
+        step()
     return g
 
 
@@ -642,6 +693,8 @@ def main():
     ap.add_argument("--workload", default="layerset")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--launch", choices=["chain", "per-gemv"], default="chain",
+                    help="one-token GEMVs on one GPU: one persistent launch per step (chain) or one launch per GEMV")
     ap.add_argument("--no-token-check", action="store_true",
                     help="decode: skip comparing 64 greedy tokens with the reference engine")
     ap.add_argument("--layers", type=int, default=NLAYERS,
@@ -713,8 +766,13 @@ def main():
 
     lm = wl.startswith("lmhead")
     chain = wl == "layerchain"
+    # one token per GEMV on one GPU: the whole step as one persistent launch (af_gemv_chain)
+    use_chain = (args.impl == "ours" and tp == 1 and not lm and args.launch == "chain" and
+                 all(it["x"].shape[0] == 1 for it in items if not chain))
     if chain:
-        arm = OursChain(cbufs) if args.impl == "ours" else None
+        arm = OursChain(cbufs, as_chain=use_chain) if args.impl == "ours" else None
+    elif use_chain:
+        arm = OursChainSet(items, device)
     else:
         arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
     if args.impl == "reference":
@@ -752,7 +810,10 @@ def main():
     clocks = sampler.summary(t0, t1) if sampler else None
     ms_step = ms / args.steps
     value = total_bytes / (ms_step / 1e3) / 1e9
-    launches = len(items) * args.steps * (arm.launches_per_layer if chain else 1)
+    if use_chain:
+        launches = args.steps            # one persistent launch per step
+    else:
+        launches = len(items) * args.steps * (arm.launches_per_layer if chain else 1)
 
     e2e = None
     if not args.no_e2e and chain:
@@ -766,7 +827,7 @@ def main():
         e2e = {"value": round(total_bytes / (ems / args.steps / 1e3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(ems / args.steps, 5), "h2d_bytes_per_step": int(x_host.numel() * 2),
                "d2h_bytes_per_step": int(x_back.numel() * 2),
-               "path": "af_rmsnorm_w8a16_gemv / af_w8a16_gemv_residual / af_rmsnorm_w8a16_swiglu C ABI; residual "
+               "path": ("af_gemv_chain (one launch)" if use_chain else "af_rmsnorm_w8a16_gemv / af_w8a16_gemv_residual / af_rmsnorm_w8a16_swiglu") + " C ABI; residual "
                        "stream pinned host -> device -> pinned host each step; CUDA graph"}
     elif not args.no_e2e:
         # End to end through the C ABI with host buffers: every step copies all
@@ -791,6 +852,12 @@ def main():
                 i = it["_i"]
                 arm.launch(stream_, it, xs_dev[xo[i]:].data_ptr(), ys_dev[yo[i]:].data_ptr())
 
+        if use_chain:
+            def _all(stream_, items_):
+                arm.launch_all(stream_, items_, [xs_dev[xo[i]:].data_ptr() for i in range(len(items_))],
+                               [ys_dev[yo[i]:].data_ptr() for i in range(len(items_))])
+            E2E.launch_all = lambda self_, stream_, items_: _all(stream_, items_)
+
         for i, it in enumerate(items):
             it["_i"] = i
 
@@ -805,7 +872,8 @@ def main():
         e2e = {"value": round(total_bytes / (ems / args.steps / 1e3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(ems / args.steps, 5),
                "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_n * ys_host.element_size()),
-               "path": ("af_lm_head_gemv" if lm else "af_w8a16_gemv") + " C ABI; pinned-host x -> device, every launch of the step, outputs -> pinned host; CUDA graph"}
+               "path": ("af_lm_head_gemv" if lm else "af_gemv_chain" if use_chain else "af_w8a16_gemv") +
+                       " C ABI; pinned-host x -> device, every GEMV of the step, outputs -> pinned host; CUDA graph"}
     if sampler:
         sampler.stop()
     if comm is not None and comm.status() != 0:
@@ -838,7 +906,9 @@ def main():
                      "traffic": traffic_from_profiles(wl, len(items)) if args.impl == "ours" else None,
                      "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
                                  "reference": "cublasGemmEx + argmax (reference)"} if lm else
-                                {"ours": "gemv_fp8_m1_kernel", "reference": "w8a16_gemv_kernel (reference)"})[args.impl],
+                                {"ours": "chain_kernel (af_gemv_chain, one persistent launch per step)" if use_chain
+                                 else "chain_kernel / gemv_fp8_m1_kernel (one launch per GEMV)",
+                                 "reference": "w8a16_gemv_kernel (reference)"})[args.impl],
                      "per_launch": f"{step_bytes / (launches / args.steps) / 1e6:.2f} MB avg algorithmic bytes / launch "
                                    f"over {ms_step * 1e3 / (launches / args.steps):.2f} us avg launch (CUDA events "
                                    f"over the timed region)"},

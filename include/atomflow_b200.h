@@ -57,7 +57,8 @@ typedef enum af_argmax_mode {
 /* Fault bits a kernel records on its device instead of faulting the GPU. */
 typedef enum af_fault_bits {
     AF_FAULT_X_COPY = 1,      /* a GEMV's bounded wait for its x copy ran out (that y is invalid) */
-    AF_FAULT_POSITION = 2     /* a decode kernel read a position outside [0, max_seq) and skipped its work */
+    AF_FAULT_POSITION = 2,    /* a decode kernel read a position outside [0, max_seq) and skipped its work */
+    AF_FAULT_CHAIN_WAIT = 4   /* a projection chain's bounded wait ran out (that launch's outputs are invalid) */
 } af_fault_bits;
 
 const char* af_status_string(af_status s);
@@ -82,7 +83,9 @@ af_status af_workspace_reset(void* workspace, size_t workspace_bytes, void* stre
  *   y : FP16 [M, N] row-major          scales: see af_scale_kind
  * FP32 accumulation, FP16 round-to-nearest output.  M = 1 is the decode
  * case of the reference; 1 <= M <= 16 runs in one pass over W, larger M in
- * ceil(M/16) passes.  Returns AF_ERR_INVALID for group_size != 128 with
+ * ceil(M/16) passes.  M = 1 with group scales (the reference's decode GEMV)
+ * runs the chain kernel (af_gemv_chain) and is bit-identical to the
+ * reference's w8a16_gemv_kernel.  Returns AF_ERR_INVALID for group_size != 128 with
  * AF_SCALE_GROUP_F16, or K % 128 != 0 with group scales (the reference kernel
  * hard-codes 128-wide groups, qkv_gemm.cu:70). */
 size_t af_w8a16_gemv_workspace_bytes(int M, int N, int K, af_scale_kind kind);
@@ -223,6 +226,58 @@ af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float*
                                    int head_dim, int max_seq, void* workspace, size_t workspace_bytes, void* stream);
 af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream);
 af_status af_decode_advance(int* d_pos, int by, void* stream);
+
+/* ---------------------------------------------------- projection chains ---
+ * A sequence of one-token FP8 projections -- a decode layer's, or a whole
+ * step's -- in ONE persistent launch (one CTA per SM).  Outputs are
+ * bit-identical to the reference's w8a16_gemv_kernel (src/kernel/qkv_gemm.cu:
+ * 32-111: its per-thread FMA chains, shuffle tree and warp-order sum are
+ * reproduced exactly) followed by its element-wise kernels (rmsnorm.cu,
+ * swiglu.cu, residual_add.cu), so a chain computes what the reference's
+ * engine.cu:292-483 computes, without the kernel boundaries: while op i
+ * waits for op i-1's output, the weights of op i are already streaming.
+ *   AF_OP_GEMV           y = half(W x)
+ *   AF_OP_GEMV_RESIDUAL  y = half(y + half(W x))                       (O, down)
+ *   AF_OP_RMSNORM_GEMV   xn = half(x * r * norm_w), y = half(W xn)       (QKV)
+ *   AF_OP_RMSNORM_SWIGLU y = half(silu(half(W xn)) * half(W2 xn))        (gate/up)
+ *     r = 1 / sqrt(sum(x^2) / K + eps) in the reference's arithmetic.
+ * Each op: FP8-E4M3 W [N, K] with FP16 group scales [N, K/128]; x FP16 [K];
+ * y FP16 [N]; K % 128 == 0, K <= 16384; x, W (and W2) 16-byte aligned, scales
+ * and y 2-byte aligned, norm_w FP32 [K] 4-byte aligned, xn_out and aux
+ * (optional stage outputs, for checking) 2-byte aligned.  wait_prev != 0: the op
+ * reads data an earlier op of the chain writes, so it starts only when every
+ * CTA has finished the previous op (a device-side counter; ops before it
+ * complete first).  x may alias an earlier op's y; y of a residual op is read
+ * and written in place.  At most 320 ops per call.
+ * Workspace: af_chain_workspace_bytes(n_ops) bytes, zeroed once
+ * (af_workspace_reset) and left zeroed by every launch; needed only when some
+ * op waits (else NULL).  Calls sharing a workspace must not overlap on the GPU.
+ * Every wait is bounded: AF_FAULT_CHAIN_WAIT (af_device_faults) marks a launch
+ * whose outputs are invalid. */
+typedef enum af_op_kind {
+    AF_OP_GEMV = 0,
+    AF_OP_GEMV_RESIDUAL = 1,
+    AF_OP_RMSNORM_GEMV = 2,
+    AF_OP_RMSNORM_SWIGLU = 3
+} af_op_kind;
+typedef struct af_chain_op {
+    int kind;                 /* af_op_kind */
+    int N, K;
+    int wait_prev;
+    const void* x;
+    const void* w;
+    const void* scales;
+    const void* w2;           /* SwiGLU: the up projection's weights and scales */
+    const void* scales2;
+    const float* norm_w;      /* RMSNorm ops */
+    float eps;
+    void* y;
+    void* xn_out;             /* RMSNorm ops, optional: the normalised x FP16 [K] */
+    void* aux;                /* optional: residual op: half(W x) [N] before the add;
+                                 SwiGLU: half(gate) [N] then half(up) [N] */
+} af_chain_op;
+size_t af_chain_workspace_bytes(int n_ops);
+af_status af_gemv_chain(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for

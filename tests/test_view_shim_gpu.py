@@ -47,7 +47,7 @@ def test_launch_argmax_and_linear_gemm_view():
     lv = make_view(vd.data_ptr(), DataType.FP32, [1, V])
     st = torch.cuda.current_stream().cuda_stream
     # default: the reference launcher's result, ids < 65536 only (argmax.cu:72-73, 115-117)
-    want_ref = int(np.argmax(v[0, :65536]))
+    want_ref = int(np.argmax(v.reshape(-1)[:65536]))
     L.launch_argmax(ctypes.byref(lv), ctypes.c_void_p(out.data_ptr()), st)
     torch.cuda.synchronize()
     assert L.af_view_last_status() == 0 and int(out.item()) == want_ref

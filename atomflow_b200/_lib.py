@@ -93,7 +93,7 @@ C_SYMBOLS = {
     "af_embed_lookup": (_i, [_vp, _vp, _vp, _i, _vp]),
     "af_rope_tables": (_i, [_vp, _vp, _i, _i, ctypes.c_float]),
     "af_rope_kv_write": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
-    "af_decode_attention_workspace_bytes": (_sz, [_i, _i]),
+    "af_decode_attention_workspace_bytes": (_sz, [_i, _i, _i]),
     "af_decode_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "af_decode_rope_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "af_device_faults": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
@@ -101,6 +101,7 @@ C_SYMBOLS = {
     "af_decode_advance": (_i, [_vp, _i, _vp]),
     "af_chain_workspace_bytes": (_sz, [_i]),
     "af_gemv_chain": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
+    "af_gemv_chain_fast": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
     "af_view_last_status": (_i, []),
     "af_view_set_argmax_mode": (_i, [_i]),
 }

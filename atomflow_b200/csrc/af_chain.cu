@@ -54,11 +54,21 @@ __device__ unsigned int g_chain_faults;
 namespace af {
 namespace {
 
-constexpr int kCWarps = 8;                  // consumer warps: the reference's 256 threads
+constexpr int kRefWarps = 8;                // the reference kernel's 256 threads
+constexpr int kCWarps = 8;                  // consumer warps: thread t plays the reference's thread t
 constexpr int kThreads = (kCWarps + 1) * 32;  // + one producer warp
 constexpr int kRows = 16;                   // rows per stage
-constexpr int kBlk = 1024;                  // positions per stage (the reference's j-stride)
-constexpr int kStage = kRows * kBlk;        // bytes per stage
+constexpr int kBlk = 1024;                  // the reference's j-stride (positions)
+constexpr int kBPS = 3;                     // j-blocks per stage: 3 KB row copies (TMA bulk copies of
+                                            // 1-2 KB cannot keep HBM busy; >= 3 KB per copy can)
+constexpr int kRowB = kBlk * kBPS;          // bytes of a row in a stage
+// stage row pitch: the exact consumers read 4 consecutive bytes per lane (any
+// pitch is conflict-free); the tensor-core consumers read 16-byte pieces of rows
+// g and g + 1 in one quarter-warp, so their rows sit 16 bytes apart modulo 128
+template <bool EXACT>
+__host__ __device__ constexpr int pitch() { return EXACT ? kRowB : kRowB + 16; }
+template <bool EXACT>
+__host__ __device__ constexpr int stage_bytes() { return kRows * pitch<EXACT>(); }
 constexpr int kMaxOps = 320;
 constexpr int kMaxK = 16384;
 constexpr size_t kSmemCap = 227 * 1024;
@@ -76,19 +86,28 @@ struct Op {
     __half* xn_out;
     __half* aux;
     int kind, N, K, wait;
+    int unused;
     float eps;
 };
 
 struct Params {
     int n_ops;
     int stages;                 // ring stages
-    int x_bytes, sc_bytes;      // shared carve-up: x [K] FP16, one scale buffer
+    int x_bytes, sc_bytes;      // shared carve-up: x [K] FP16, one staged-scale buffer (two of them),
+    int sct_bytes;              // and the transposed scales of the current op
     int* counters;              // [n_ops + 1] completion counters (null: no op waits)
     unsigned long long wait_ns;
     Op ops[kMaxOps];
 };
 
 static_assert(sizeof(Params) <= 32764, "the op table must fit the kernel parameter space");
+
+// One more finished tile: a release add, so the tile's output rows (stored by
+// this warp before the __syncwarp that precedes it) are visible to whoever
+// acquires the count.
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+    asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
     int v;
@@ -112,6 +131,29 @@ __device__ __forceinline__ void fma_pair(float& s0, float& s1, float a0, float a
     asm("mov.b64 %0, {%1,%1};" : "=l"(xv) : "f"(x));
     asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(sv) : "l"(av), "l"(xv));
     asm("mov.b64 {%0,%1}, %2;" : "=f"(s0), "=f"(s1) : "l"(sv));
+}
+
+// Shared-memory loads by 32-bit shared address (volatile: a ring slot's
+// contents change between the mbarrier phases that guard it).
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint16_t lds16(uint32_t a) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
 }
 
 // Bounded mbarrier wait that gives up at once when the CTA has aborted.
@@ -152,14 +194,29 @@ __device__ __forceinline__ ScaleLayout scale_layout(const Op& op, const RowSplit
     return sl;
 }
 
+// EXACT: the reference's arithmetic, bit for bit.  !EXACT: the same data flow
+// with the dot products on the tensor cores (FP8 -> FP16 packed conversion,
+// m16n8k16 MMAs with FP32 accumulation, the group scale applied to each
+// 128-position group sum, warps combined in a fixed order): deterministic, and
+// within the FP16 rounding of FP64, but not the reference's summation order.
+template <bool EXACT>
 __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(1024) unsigned char smem[];
+    constexpr int kStage = stage_bytes<EXACT>();
+    constexpr int kPitch = pitch<EXACT>();
     const int S = p.stages;
     unsigned char* ring = smem;
     __half* xs = reinterpret_cast<__half*>(smem + (size_t)S * kStage);
     unsigned char* scb = reinterpret_cast<unsigned char*>(xs) + p.x_bytes;
+    uint16_t* sct = reinterpret_cast<uint16_t*>(scb + 2 * (size_t)p.sc_bytes);   // [m][G][rows_pad]
     __shared__ __align__(8) uint64_t full[16], empty[16], sc_full[2], sc_empty[2];
-    __shared__ float part[2][kCWarps][kRows];
+    // warp sums of the last 8 tiles: consumer warps run at most one ring (<= 6
+    // stages, >= 1 stage per tile) apart, so a tile's buffer is free again
+    // before any warp reaches the tile 8 later
+    __shared__ float part[8][kRefWarps][kRows];
+    __shared__ int s_tcnt[8];                       // warps done with each of them
+    __shared__ int s_opdone[2];                     // tiles of the current op finished (op parity)
+    __shared__ __align__(16) uint32_t s_zero[64];   // B fragments of the MMA columns that carry no token
     __shared__ float s_nrm[4];
     __shared__ float s_r;
     __shared__ volatile int s_abort;
@@ -175,6 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
             mbar_init(smem_u32(&sc_empty[b]), kCWarps);
         }
         s_abort = 0;
+        for (int i = 0; i < 8; ++i) s_tcnt[i] = 0;
+        s_opdone[0] = s_opdone[1] = 0;
+        for (int i = 0; i < 64; ++i) s_zero[i] = 0;
         mbar_init_fence();
     }
     __syncthreads();
@@ -185,7 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         int slot = 0;
         uint32_t phase = 0;
         int issued = 0;
-        for (int o = 0; o < p.n_ops && !s_abort; ++o) {
+        // this CTA's group scales of op o -> scale buffer o & 1 (issued one op
+        // ahead, so that waiting on its plain loads never holds up the weights)
+        auto stage_scales = [&](int o) {
             const Op& op = p.ops[o];
             const RowSplit rs = row_split(op);
             const bool pair = op.kind == OP_RMSNORM_SWIGLU;
@@ -226,14 +288,20 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                 (void)tx;
                 mbar_arrive(scf);   // 32 arrivals, each lane after its own stores; plus the bulk bytes
             }
+        };
+        stage_scales(0);
+        for (int o = 0; o < p.n_ops && !s_abort; ++o) {
+            const Op& op = p.ops[o];
+            const RowSplit rs = row_split(op);
+            const bool pair = op.kind == OP_RMSNORM_SWIGLU;
 
-            const int nblk = (op.K + kBlk - 1) / kBlk;
+            const int nst = (op.K + kRowB - 1) / kRowB;   // stages per 16-row tile
             for (int tr = rs.r0; tr < rs.r1; tr += rs.tr) {
                 const int nv = min(rs.tr, rs.r1 - tr);
-                for (int j = 0; j < nblk; ++j) {
+                for (int j = 0; j < nst; ++j) {
                     chain_wait(smem_u32(&empty[slot]), phase ^ 1, p.wait_ns, &s_abort);
                     if (s_abort) break;
-                    const int bb = min(kBlk, op.K - j * kBlk);
+                    const int bb = min(kRowB, op.K - j * kRowB);
                     const uint32_t fb = smem_u32(&full[slot]);
                     if (lane == 0) mbar_arrive_expect_tx(fb, (uint32_t)((pair ? 2 * nv : nv) * bb));
                     __syncwarp();
@@ -241,11 +309,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                         const uint8_t* src = nullptr;
                         if (pair) {
                             const int r = lane & 7;
-                            if (r < nv) src = (lane < 8 ? op.w : op.w2) + (size_t)(tr + r) * op.K + (size_t)j * kBlk;
+                            if (r < nv) src = (lane < 8 ? op.w : op.w2) + (size_t)(tr + r) * op.K + (size_t)j * kRowB;
                         } else if (lane < nv) {
-                            src = op.w + (size_t)(tr + lane) * op.K + (size_t)j * kBlk;
+                            src = op.w + (size_t)(tr + lane) * op.K + (size_t)j * kRowB;
                         }
-                        if (src) bulk_g2s(smem_u32(ring + (size_t)slot * kStage + lane * kBlk), src, (uint32_t)bb, fb);
+                        if (src) bulk_g2s(smem_u32(ring + (size_t)slot * kStage + lane * kPitch), src, (uint32_t)bb, fb);
                     }
                     ++issued;
                     if (++slot == S) {
@@ -255,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                 }
                 if (s_abort) break;
             }
+            if (o + 1 < p.n_ops && !s_abort) stage_scales(o + 1);
         }
         if (s_abort && lane == 0) {
             // a wait gave up: the copies already issued still land in this CTA's
@@ -269,33 +338,49 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         }
     } else {
         // ------------------------------------------------------------ consumers
-        const int t = threadIdx.x;   // the reference's thread index
+        const int ct = threadIdx.x;                 // consumer thread
+        const int t = ct;                           // = the reference's thread index
         pdl_wait();                  // x / residual inputs of the first ops may come from the previous kernel
         int slot = 0;
         uint32_t phase = 0;
         int tb = 0;
+        bool ready = false;   // the next stage's full barrier tested complete
         for (int o = 0; o < p.n_ops; ++o) {
             const Op& op = p.ops[o];
             const RowSplit rs = row_split(op);
             const bool pair = op.kind == OP_RMSNORM_SWIGLU;
             const int G = op.K >> 7;
             const int K = op.K;
-            if (op.wait && o > 0 && p.counters != nullptr) {
+            if (o > 0) named_bar_sync(1, kCWarps * 32);   // every warp is done with the previous op's x and scales
+            // this CTA's scales of the op: [rows][G] -> [G][rows_pad] (gate's, then up's), so
+            // that a thread's 16 stage rows at one group are 32 contiguous bytes -- done
+            // before the dependency wait, which it does not need
+            const int b = o & 1;
+            chain_wait(smem_u32(&sc_full[b]), (o >> 1) & 1, p.wait_ns, &s_abort);
+            const ScaleLayout sl = scale_layout(op, rs, G);
+            const int rows = rs.r1 - rs.r0, rows_pad = (rows + 15) & ~15;
+            for (int m = 0; m < (pair ? 2 : 1); ++m) {
+                const uint16_t* src = reinterpret_cast<const uint16_t*>(scb + (size_t)b * p.sc_bytes + sl.off[m]);
+                uint16_t* dst = sct + (size_t)m * G * rows_pad;
+                for (int i = ct; i < rows * G; i += kCWarps * 32) {
+                    const int r = i / G, gg = i - r * G;
+                    dst[gg * rows_pad + r] = src[i];
+                }
+            }
+            if (op.wait && o > 0 && p.counters != nullptr && ct == 0 && !s_abort) {
                 // op o reads what op o-1 wrote: wait until every CTA has finished it
-                if (t == 0 && !s_abort) {
-                    const unsigned long long t0 = globaltimer_ns();
-                    while (ld_acquire_gpu(p.counters + o - 1) < (int)gridDim.x) {
-                        if (globaltimer_ns() - t0 > p.wait_ns) {
-                            atomicOr(&g_chain_faults, (unsigned)AF_FAULT_CHAIN_WAIT);
-                            s_abort = 1;
-                            break;
-                        }
+                const unsigned long long t0 = globaltimer_ns();
+                while (ld_acquire_gpu(p.counters + o - 1) < (int)gridDim.x) {
+                    if (globaltimer_ns() - t0 > p.wait_ns) {
+                        atomicOr(&g_chain_faults, (unsigned)AF_FAULT_CHAIN_WAIT);
+                        s_abort = 1;
+                        break;
                     }
                 }
-                named_bar_sync(1, kCWarps * 32);
             }
+            named_bar_sync(1, kCWarps * 32);
             // x -> shared (L2-coherent loads: another CTA may have written it)
-            for (int i = t * 8; i < K; i += kCWarps * 32 * 8)
+            for (int i = ct * 8; i < K; i += kCWarps * 32 * 8)
                 *reinterpret_cast<uint4*>(xs + i) = ldcg_u4(op.x + i);
             named_bar_sync(1, kCWarps * 32);
             if (op.kind == OP_RMSNORM_GEMV || op.kind == OP_RMSNORM_SWIGLU) {
@@ -303,9 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                 // 128 threads): strided FMA sums, shuffle-down tree 1..16, the four
                 // warp sums in order, rsqrt(sum / K + eps) as its fast-math build
                 // evaluates it, then half(x * r * w).
-                if (t < 128) {
+                if (ct < 128) {
                     float ss = 0.f;
-                    for (int i = t; i < K; i += 128) {
+                    for (int i = ct; i < K; i += 128) {
                         const float v = __half2float(xs[i]);
                         ss = fmaf(v, v, ss);
                     }
@@ -314,59 +399,65 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                     if (lane == 0) s_nrm[warp] = ss;
                 }
                 named_bar_sync(1, kCWarps * 32);
-                if (t == 0) s_r = rms_scale_ref(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], K, op.eps);
+                if (ct == 0) s_r = rms_scale_ref(((s_nrm[0] + s_nrm[1]) + s_nrm[2]) + s_nrm[3], K, op.eps);
                 named_bar_sync(1, kCWarps * 32);
                 const float r = s_r;
-                for (int i = t; i < K; i += kCWarps * 32)
+                for (int i = ct; i < K; i += kCWarps * 32)
                     xs[i] = __float2half_rn(__half2float(xs[i]) * r * __ldg(op.norm_w + i));
                 named_bar_sync(1, kCWarps * 32);
                 if (op.xn_out != nullptr && blockIdx.x == 0)
-                    for (int i = t; i < K; i += kCWarps * 32) op.xn_out[i] = xs[i];
+                    for (int i = ct; i < K; i += kCWarps * 32) op.xn_out[i] = xs[i];
             }
-            const int b = o & 1;
-            chain_wait(smem_u32(&sc_full[b]), (o >> 1) & 1, p.wait_ns, &s_abort);
-            const ScaleLayout sl = scale_layout(op, rs, G);
-            const uint16_t* sc = reinterpret_cast<const uint16_t*>(scb + (size_t)b * p.sc_bytes + sl.off[0]);
-            const int up_base = (sl.off[1] - sl.off[0]) / 2;   // halves from gate's block to up's
+            const uint32_t sct_u = smem_u32(sct);
+            const uint32_t up_off = (uint32_t)G * rows_pad * 2;   // bytes from gate's block to up's
+            const uint32_t ring_u = smem_u32(ring) + 4 * t;   // exact path: thread t's 4 bytes of a row
+            const uint32_t ring_m = smem_u32(ring);
+            const uint32_t xs_u = smem_u32(xs);
 
-            const int nblk = (K + kBlk - 1) / kBlk;
             for (int tr = rs.r0; tr < rs.r1; tr += rs.tr) {
                 const int nv = min(rs.tr, rs.r1 - tr);
-                // the 16 stage rows' scale rows in the staged block (invalid rows: row 0's)
-                int srow[kRows];
-#pragma unroll
-                for (int i = 0; i < kRows; ++i) {
-                    const int r = pair ? (i & 7) : i;
-                    const int rr = (r < nv ? tr + r : tr) - rs.r0;
-                    srow[i] = (pair && i >= 8 ? up_base : 0) + rr * G;
-                }
+                const uint32_t toff = (uint32_t)(tr - rs.r0) * 2;   // this tile's rows in a transposed group row
+                if constexpr (EXACT) {
                 float acc[kRows];
 #pragma unroll
                 for (int i = 0; i < kRows; ++i) acc[i] = 0.f;
-                for (int j = 0; j < nblk; ++j) {
-                    chain_wait(smem_u32(&full[slot]), phase, p.wait_ns, &s_abort);
-                    const int kp = j * kBlk + 4 * t;
-                    if (kp < K) {
-                        const uint2 xr = *reinterpret_cast<const uint2*>(xs + kp);
-                        const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&xr.x));
-                        const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&xr.y));
-                        const int gidx = kp >> 7;
-                        const unsigned char* st = ring + (size_t)slot * kStage + 4 * t;
+                const int nst = (K + kRowB - 1) / kRowB;
+                for (int j = 0; j < nst; ++j) {
+                    // the stage's full barrier was tested (non-blocking) while the
+                    // previous stage was computed; wait only if it was not complete
+                    if (!ready) chain_wait(smem_u32(&full[slot]), phase, p.wait_ns, &s_abort);
+                    {
+                        const int ns = slot + 1 == S ? 0 : slot + 1;
+                        ready = mbar_test_wait(smem_u32(&full[ns]), ns == 0 ? phase ^ 1 : phase);
+                    }
+                    const uint32_t st = ring_u + (uint32_t)slot * kStage;
 #pragma unroll
-                        for (int i = 0; i < kRows; i += 2) {
-                            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(st + i * kBlk);
-                            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(st + (i + 1) * kBlk);
-                            const uint16_t s0 = sc[srow[i] + gidx], s1 = sc[srow[i + 1] + gidx];
-                            const uint32_t h0a = e4m3x2_lo(w0), h0b = e4m3x2_hi(w0);
-                            const uint32_t h1a = e4m3x2_lo(w1), h1b = e4m3x2_hi(w1);
-                            fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)h0a, s0),
-                                     mul_f16_exact((uint16_t)h1a, s1), x01.x);
-                            fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)(h0a >> 16), s0),
-                                     mul_f16_exact((uint16_t)(h1a >> 16), s1), x01.y);
-                            fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)h0b, s0),
-                                     mul_f16_exact((uint16_t)h1b, s1), x23.x);
-                            fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)(h0b >> 16), s0),
-                                     mul_f16_exact((uint16_t)(h1b >> 16), s1), x23.y);
+                    for (int jb = 0; jb < kBPS; ++jb) {
+                        const int kp = (j * kBPS + jb) * kBlk + 4 * t;   // the reference's kv for this j
+                        if (kp < K) {
+                            const uint2 xr = lds64(xs_u + 2 * kp);
+                            const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&xr.x));
+                            const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&xr.y));
+                            const uint32_t sa = sct_u + (uint32_t)(kp >> 7) * rows_pad * 2 + toff;
+                            const uint4 sv0 = lds128(sa);                          // rows 0-7 (gate's for SwiGLU)
+                            const uint4 sv1 = lds128(pair ? sa + up_off : sa + 16);  // rows 8-15 (up's for SwiGLU)
+                            const uint32_t sw[8] = {sv0.x, sv0.y, sv0.z, sv0.w, sv1.x, sv1.y, sv1.z, sv1.w};
+#pragma unroll
+                            for (int i = 0; i < kRows; i += 2) {
+                                const uint32_t w0 = lds32(st + i * kRowB + jb * kBlk);
+                                const uint32_t w1 = lds32(st + (i + 1) * kRowB + jb * kBlk);
+                                const uint16_t s0 = (uint16_t)(sw[i >> 1] & 0xffffu), s1 = (uint16_t)(sw[i >> 1] >> 16);
+                                const uint32_t h0a = e4m3x2_lo(w0), h0b = e4m3x2_hi(w0);
+                                const uint32_t h1a = e4m3x2_lo(w1), h1b = e4m3x2_hi(w1);
+                                fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)h0a, s0),
+                                         mul_f16_exact((uint16_t)h1a, s1), x01.x);
+                                fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)(h0a >> 16), s0),
+                                         mul_f16_exact((uint16_t)(h1a >> 16), s1), x01.y);
+                                fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)h0b, s0),
+                                         mul_f16_exact((uint16_t)h1b, s1), x23.x);
+                                fma_pair(acc[i], acc[i + 1], mul_f16_exact((uint16_t)(h0b >> 16), s0),
+                                         mul_f16_exact((uint16_t)(h1b >> 16), s1), x23.y);
+                            }
                         }
                     }
                     __syncwarp();
@@ -416,45 +507,120 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                 const int rowof = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
                                   ((lane >> 1) & 1);
                 if ((lane & 1) == 0) part[tb][warp][rowof] = v1;
-                named_bar_sync(1, kCWarps * 32);
-                // the warp sums in warp order, from 0.0f, then the op's epilogue
-                if (t < (pair ? 8 : 16) && t < nv) {
-                    float tot = 0.f;
+                } else {
+                // tensor-core path: warp w takes positions [384 w, 384 w + 384) of
+                // each stage (three scale groups); lane (g, c) feeds rows g and g + 8
+                const int g = lane >> 2, c = lane & 3;
+                float acc0 = 0.f, acc1 = 0.f;   // rows g, g + 8 (column 0 of the MMA: lanes c == 0)
+                const uint32_t xlane = g == 0 ? xs_u + 64 * c : smem_u32(s_zero);   // columns 1..7 carry zeros
+                const uint32_t xstep = g == 0 ? 1u : 0u;
+                const uint32_t srow0 = toff + 2 * g;                         // row g's scale in a transposed group row
+                const uint32_t srow1 = pair ? up_off + toff + 2 * g : toff + 2 * (g + 8);
+                const int nst = (K + kRowB - 1) / kRowB;
+                for (int j = 0; j < nst; ++j) {
+                    if (!ready) chain_wait(smem_u32(&full[slot]), phase, p.wait_ns, &s_abort);
+                    {
+                        const int ns = slot + 1 == S ? 0 : slot + 1;
+                        ready = mbar_test_wait(smem_u32(&full[ns]), ns == 0 ? phase ^ 1 : phase);
+                    }
+                    const uint32_t rowg =
+                        ring_m + (uint32_t)slot * kStage + (uint32_t)g * kPitch + warp * (kBPS * 128) + c * 32;
 #pragma unroll
-                    for (int w = 0; w < kCWarps; ++w) tot += part[tb][w][t];
-                    const int row = tr + t;
-                    if (pair) {
-                        float up = 0.f;
+                    for (int gg = 0; gg < kBPS; ++gg) {
+                        const int gp = j * kRowB + warp * (kBPS * 128) + gg * 128;   // the group's first position
+                        if (gp < K) {
+                            const uint32_t ra = rowg + gg * 128;
+                            const uint4 r0a = lds128(ra), r0b = lds128(ra + 16);
+                            const uint4 r1a = lds128(ra + 8 * kPitch), r1b = lds128(ra + 8 * kPitch + 16);
+                            const uint32_t xa = xlane + xstep * 2u * (uint32_t)gp;
+                            const uint4 xq0 = lds128(xa), xq1 = lds128(xa + 16), xq2 = lds128(xa + 32),
+                                        xq3 = lds128(xa + 48);
+                            const uint32_t w0[8] = {r0a.x, r0a.y, r0a.z, r0a.w, r0b.x, r0b.y, r0b.z, r0b.w};
+                            const uint32_t w1[8] = {r1a.x, r1a.y, r1a.z, r1a.w, r1b.x, r1b.y, r1b.z, r1b.w};
+                            const uint32_t xw[16] = {xq0.x, xq0.y, xq0.z, xq0.w, xq1.x, xq1.y, xq1.z, xq1.w,
+                                                     xq2.x, xq2.y, xq2.z, xq2.w, xq3.x, xq3.y, xq3.z, xq3.w};
+                            float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int w = 0; w < kCWarps; ++w) up += part[tb][w][8 + t];
-                        // swiglu.cu:12-26 on the FP16 gate / up outputs
-                        const __half gh = __float2half_rn(tot), uh = __float2half_rn(up);
-                        if (op.aux != nullptr) {
-                            op.aux[row] = gh;
-                            op.aux[op.N + row] = uh;
+                            for (int m = 0; m < 8; ++m)
+                                mma16816(d, e4m3x2_lo(w0[m]), e4m3x2_lo(w1[m]), e4m3x2_hi(w0[m]), e4m3x2_hi(w1[m]),
+                                         xw[2 * m], xw[2 * m + 1]);
+                            const uint32_t sg = sct_u + (uint32_t)(gp >> 7) * rows_pad * 2;
+                            acc0 = fmaf(half_bits_to_float(lds16(sg + srow0)), d[0], acc0);
+                            acc1 = fmaf(half_bits_to_float(lds16(sg + srow1)), d[2], acc1);
                         }
-                        const float g = __half2float(gh);
-                        const float u = __half2float(uh);
-                        const float silu = fdiv_full_ftz(g, 1.0f + __expf(-g));
-                        op.y[row] = __float2half_rn(silu * u);
-                    } else if (op.kind == OP_GEMV_RESIDUAL) {
-                        // residual_add.cu:11-20: half(float(x) + float(half(Wx)))
-                        const unsigned short old = __ldcg(reinterpret_cast<const unsigned short*>(op.y) + row);
-                        const __half oh = __float2half_rn(tot);
-                        if (op.aux != nullptr) op.aux[row] = oh;
-                        const float o16 = __half2float(oh);
-                        op.y[row] = __float2half_rn(half_bits_to_float(old) + o16);
-                    } else {
-                        op.y[row] = __float2half_rn(tot);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
+                    if (++slot == S) {
+                        slot = 0;
+                        phase ^= 1;
                     }
                 }
-                tb ^= 1;
+                if (c == 0) {
+                    part[tb][warp][g] = acc0;
+                    part[tb][warp][g + 8] = acc1;
+                }
+                }
+                // the last warp done with the tile finishes it (no CTA-wide barrier per tile)
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    __threadfence_block();
+                    last = atomicAdd(&s_tcnt[tb], 1) == kCWarps - 1;
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence_block();
+                    if (lane < (pair ? 8 : 16) && lane < nv) {
+                        // the warp sums in warp order, from 0.0f, then the op's epilogue
+                        float tot = 0.f;
+#pragma unroll
+                        for (int w = 0; w < kRefWarps; ++w) tot += part[tb][w][lane];
+                        const int row = tr + lane;
+                        if (pair) {
+                            float up = 0.f;
+#pragma unroll
+                            for (int w = 0; w < kRefWarps; ++w) up += part[tb][w][8 + lane];
+                            // swiglu.cu:12-26 on the FP16 gate / up outputs
+                            const __half gh = __float2half_rn(tot), uh = __float2half_rn(up);
+                            if (op.aux != nullptr) {
+                                op.aux[row] = gh;
+                                op.aux[op.N + row] = uh;
+                            }
+                            const float g = __half2float(gh);
+                            const float u = __half2float(uh);
+                            const float silu = fdiv_full_ftz(g, 1.0f + __expf(-g));
+                            op.y[row] = __float2half_rn(silu * u);
+                        } else if (op.kind == OP_GEMV_RESIDUAL) {
+                            // residual_add.cu:11-20: half(float(x) + float(half(Wx)))
+                            const unsigned short old = __ldcg(reinterpret_cast<const unsigned short*>(op.y) + row);
+                            const __half oh = __float2half_rn(tot);
+                            if (op.aux != nullptr) op.aux[row] = oh;
+                            const float o16 = __half2float(oh);
+                            op.y[row] = __float2half_rn(half_bits_to_float(old) + o16);
+                        } else {
+                            op.y[row] = __float2half_rn(tot);
+                        }
+                    }
+                    __syncwarp();   // the tile's rows are stored
+                    if (lane == 0) {
+                        s_tcnt[tb] = 0;
+                        // count the tile in the CTA (release at CTA scope: the warp's row
+                        // stores come first); the CTA's last tile of the op publishes the
+                        // CTA's rows with one GPU-scope release add
+                        __threadfence_block();
+                        const int ntiles = (rs.r1 - rs.r0 + rs.tr - 1) / rs.tr;
+                        if (atomicAdd(&s_opdone[o & 1], 1) == ntiles - 1) {
+                            __threadfence_block();   // acquire the CTA's other tiles
+                            s_opdone[o & 1] = 0;
+                            if (p.counters != nullptr) red_release_gpu_add(p.counters + o, 1);
+                        }
+                    }
+                }
+                tb = (tb + 1) & 7;
             }
-            named_bar_sync(1, kCWarps * 32);   // every row of this op is stored
-            if (t == 0 && p.counters != nullptr) {
-                __threadfence();
-                atomicAdd(p.counters + o, 1);
-            }
+            // a CTA without rows in this op still reports it done
+            if (rs.r1 == rs.r0 && ct == 0 && p.counters != nullptr) red_release_gpu_add(p.counters + o, 1);
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&sc_empty[b]));
         }
@@ -504,12 +670,12 @@ struct Attr {
     std::once_flag once;
     cudaError_t err = cudaSuccess;
 };
-Attr g_attr[kMaxDevices];
+Attr g_attr[kMaxDevices * 2];
 
 }  // namespace
 
 af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_t ws_bytes, cudaStream_t st,
-                       bool single) {
+                       bool single, bool exact) {
     if (ops == nullptr || n_ops <= 0 || n_ops > kMaxOps) return n_ops > kMaxOps ? AF_ERR_UNSUPPORTED : AF_ERR_INVALID;
     int dev = 0;
     const int sms = device_sm_count(&dev);
@@ -528,21 +694,30 @@ af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_
     }
     scb = round_up(scb, 128);
     xb = round_up(xb, 128);
+    size_t sctb = 128;
+    for (int o = 0; o < n_ops; ++o) {
+        const size_t rows = ((size_t)ops[o].N + sms - 1) / sms;
+        sctb = std::max(sctb, ((rows + 15) / 16 * 16) * (ops[o].K / 128) * 2 *
+                                  (ops[o].kind == AF_OP_RMSNORM_SWIGLU ? 2 : 1));
+    }
+    sctb = round_up(sctb, 128);
     if (waits) {
         if (workspace == nullptr || ws_bytes < af_chain_workspace_bytes(n_ops)) return AF_ERR_WORKSPACE;
         if (!aligned(workspace, 4)) return AF_ERR_INVALID;
     }
-    const size_t fixed = xb + 2 * scb + 2048;   // + static shared memory and alignment
-    if (fixed + 2 * (size_t)kStage > kSmemCap) return AF_ERR_UNSUPPORTED;
-    // one projection: a 5-stage ring (two CTAs per SM, so the next kernel's CTA
+    const size_t fixed = xb + 2 * scb + sctb + 6144;   // + static shared memory and alignment
+    const size_t kStage = exact ? stage_bytes<true>() : stage_bytes<false>();
+    if (fixed + 2 * kStage > kSmemCap) return AF_ERR_UNSUPPORTED;
+    // one projection: a 3-stage ring (two CTAs per SM, so the next kernel's CTA
     // starts streaming under programmatic dependent launch); a chain: the
     // deepest ring that fits (one CTA per SM)
-    int stages = (int)std::min<size_t>(16, (kSmemCap - fixed) / kStage);
-    if (single) stages = std::min(stages, 5);
+    int stages = (int)std::min<size_t>(6, (kSmemCap - fixed) / kStage);
+    if (single) stages = std::min(stages, 3);
     prm.n_ops = n_ops;
     prm.stages = stages;
     prm.x_bytes = (int)xb;
     prm.sc_bytes = (int)scb;
+    prm.sct_bytes = (int)sctb;
     prm.counters = waits ? static_cast<int*>(workspace) : nullptr;
     prm.wait_ns = 2000000000ull;
     for (int o = 0; o < n_ops; ++o) {
@@ -561,20 +736,22 @@ af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_
         d.N = a.N;
         d.K = a.K;
         d.wait = a.wait_prev != 0;
+
         d.eps = a.eps;
     }
-    Attr& at = g_attr[dev % kMaxDevices];
+    auto kern = exact ? chain_kernel<true> : chain_kernel<false>;
+    Attr& at = g_attr[(dev % kMaxDevices) * 2 + (exact ? 1 : 0)];
     std::call_once(at.once, [&] {
-        at.err = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap - 2048);
+        at.err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap - 6144);
         if (at.err == cudaSuccess)
-            at.err = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+            at.err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                           (int)cudaSharedmemCarveoutMaxShared);
     });
     if (at.err != cudaSuccess) return cuda_fail(at.err, "chain_kernel attributes");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)stages * kStage + xb + 2 * scb;
+    cfg.dynamicSmemBytes = (size_t)stages * kStage + xb + 2 * scb + sctb;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     if (waits) {
@@ -587,7 +764,7 @@ af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_
     }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, chain_kernel, prm);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "chain_kernel");
 }
 
@@ -600,5 +777,12 @@ extern "C" size_t af_chain_workspace_bytes(int n_ops) {
 
 extern "C" af_status af_gemv_chain(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
                                    void* stream) {
-    return af::chain_launch(ops, n_ops, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), n_ops == 1);
+    return af::chain_launch(ops, n_ops, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), n_ops == 1,
+                            true);
+}
+
+extern "C" af_status af_gemv_chain_fast(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+    return af::chain_launch(ops, n_ops, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), n_ops == 1,
+                            false);
 }

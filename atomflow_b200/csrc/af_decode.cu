@@ -84,215 +84,178 @@ __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict
 }
 
 // ------------------------------------------------------ cached attention
-// Split-KV GQA attention for one token.  CTA (split, kv head) handles
-// positions [t0, t1) of the cache for the G = NH/NKV query heads that share
-// the kv head; each of its 8 warps takes every 8th position with an online
-// softmax (lane l holds dims 4l..4l+3; two positions' loads in flight).  The
-// CTA's partial (max, sum, o) goes to the workspace; the last CTA of the kv
-// head merges the splits in split order (deterministic) and writes out, then
-// re-zeroes its counter.  (A lane-per-position layout -- one k row per lane,
-// then p.v by dims -- was measured slower at 1-2k positions: with 32 splits
-// a CTA has ~32 positions, which left one warp doing all of them.)
-constexpr int kAttnSplits = 32;
+// GQA attention for one token, bit-identical to the reference's
+// gqa_cached_attention_kernel (src/kernel/tiled_attention.cu:196-269, built
+// with --use_fast_math), whose arithmetic per query head is:
+//   score[t] = tree_sum_d(q[d] * k[t][d]) * rsqrtf(HD)   (pairwise tree, strides 64..1)
+//   m = max_t score[t];  e[t] = expf(score[t] - m);  sum = e[0] + e[1] + ... (in t order)
+//   p[t] = e[t] * (1 / sum);  out[d] = half(sum_t p[t] * v[t][d])   (FMA chain in t order)
+// The scores are independent per position, so they are spread over the GPU:
+// CTA (chunk, kv head) scores positions [t0, t1) of the cache for the G query
+// heads sharing the kv head (one warp per position; lane l holds dims l, l+32,
+// l+64, l+96, so the reference's strides 64 and 32 are in-lane adds and
+// strides 16..1 a shuffle butterfly -- FP addition is commutative, so every
+// partial sum is the reference's).  The two order-bound sums (the softmax
+// denominator, and each output dim's chain over t) cannot be split without
+// changing the rounding: the last CTA of each kv head runs them, one
+// 128-thread group per query head, reading the scores back from the workspace.
+constexpr int kAttnChunks = 16;
 constexpr int kAttnMaxG = 8;
 
-template <int G, int kAttnWarps>
-__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(
-    const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
-    const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
-    int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
-    int form, __half* k_wr, __half* v_wr, int max_seq) {
-    // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
-    // vector: every CTA rotates its own query heads, and the current position's
-    // k (rotated) and v come from qkv in registers; the one CTA whose range
-    // holds that position also writes them to the caches (no CTA reads that row).
-    constexpr int HD = 128;
-    const int split = blockIdx.x, kvh = blockIdx.y;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (pos_out_of_range(*d_pos, max_seq)) return;
-    const int seq = *d_pos + 1;
-    const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
-    const int t0 = min(seq, split * chunk), t1 = min(seq, t0 + chunk);
-    const int kv_dim = NKV * HD;
-    const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
+// Operand order of the RoPE contraction (see rope_pair): form 0 reproduces the
+// reference's rope kernel bit for bit (tests/test_decode_gpu.py pins it; form 1
+// is the other order, kept in rope_pair for that comparison).
+constexpr int kRopeForm = 0;
+// 1 / sum in the reference's fast-math build: the approximate reciprocal
+// (form 0) or the full-range approximate division 1 / x (form 1).
+constexpr int kRecipForm = 0;
 
+__device__ __forceinline__ float recip_ref(float x) {
+    return kRecipForm == 0 ? rcp_approx_ftz(x) : fdiv_full_ftz(1.0f, x);
+}
+
+template <int G>
+__global__ void __launch_bounds__(G * 128) attention_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
+    const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ scores,
+    int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
+    int max_seq, __half* k_wr, __half* v_wr) {
+    // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
+    // vector: every CTA rotates its own query heads (rounded to FP16, as the
+    // reference stores them), the current position's k (rotated) and v come
+    // from qkv, and the CTA whose range holds that position writes them to the
+    // caches.
+    constexpr int HD = 128;
+    constexpr int NW = G * 4;
+    const int pos = *d_pos;
+    if (pos_out_of_range(pos, max_seq)) return;
+    const int seq = pos + 1;
+    const int chunk = blockIdx.x, kvh = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int kv_dim = NKV * HD;
     const bool fused = cos_tab != nullptr;
-    const int pos = seq - 1;
-    // RoPE of 4 dims held by this lane; dims d and d + HD/2 sit in lanes l and l ^ 16.
-    float rc[4], rs[4];
+
+    float rc[2] = {0.f, 0.f}, rs[2] = {0.f, 0.f};   // pair indices lane and lane + 32
     if (fused) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int d = (lane & 15) * 4 + e;
-            rc[e] = cos_tab[(size_t)pos * (HD / 2) + d];
-            rs[e] = sin_tab[(size_t)pos * (HD / 2) + d];
-        }
+        rc[0] = cos_tab[(size_t)pos * (HD / 2) + lane];
+        rs[0] = sin_tab[(size_t)pos * (HD / 2) + lane];
+        rc[1] = cos_tab[(size_t)pos * (HD / 2) + lane + 32];
+        rs[1] = sin_tab[(size_t)pos * (HD / 2) + lane + 32];
     }
-    auto rotate = [&](float (&v)[4]) {   // v: this lane's 4 dims -> rotated, rounded to FP16
+    auto ld4 = [&](const __half* base, float (&v)[4]) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-            float o0, o1;
-            // (x, y) = (dim d, dim d + HD/2): lanes < 16 own x and keep o0, the others own y and keep o1
-            if (lane < 16) rope_pair(v[e], other, rc[e], rs[e], form, o0, o1);
-            else rope_pair(other, v[e], rc[e], rs[e], form, o0, o1);
-            v[e] = __half2float(__float2half_rn(lane < 16 ? o0 : o1));
-        }
+        for (int i = 0; i < 4; ++i) v[i] = __half2float(base[lane + 32 * i]);
     };
-    auto load4 = [&](const __half* src, float (&v)[4]) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(src);
-        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
-        v[0] = __low2float(a);
-        v[1] = __high2float(a);
-        v[2] = __low2float(b);
-        v[3] = __high2float(b);
+    auto rot = [&](float (&v)[4]) {   // pairs (d, d + 64): (v0, v2) and (v1, v3)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            float o0, o1;
+            rope_pair(v[i], v[i + 2], rc[i], rs[i], kRopeForm, o0, o1);
+            v[i] = __half2float(__float2half_rn(o0));
+            v[i + 2] = __half2float(__float2half_rn(o1));
+        }
     };
     float qv[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        load4(q + (size_t)(kvh * G + g) * HD + lane * 4, qv[g]);
-        if (fused) rotate(qv[g]);
+        ld4(q + (size_t)(kvh * G + g) * HD, qv[g]);
+        if (fused) rot(qv[g]);
     }
-    float kcur[4], vcur[4];
+    const int per = (seq + kAttnChunks - 1) / kAttnChunks;
+    const int t0 = min(seq, chunk * per), t1 = min(seq, t0 + per);
+    float kcur[4] = {0.f, 0.f, 0.f, 0.f};
     if (fused) {
-        const __half* kq = q + (size_t)NH * HD + (size_t)kvh * HD + lane * 4;
-        load4(kq, kcur);
-        rotate(kcur);
-        load4(kq + (size_t)NKV * HD, vcur);
+        const __half* kq = q + (size_t)NH * HD + (size_t)kvh * HD;
+        ld4(kq, kcur);
+        rot(kcur);
         if (warp == 0 && t0 <= pos && pos < t1) {
-            const size_t row = (size_t)pos * kv_dim + (size_t)kvh * HD + lane * 4;
+            float vcur[4];
+            ld4(kq + kv_dim, vcur);
+            const size_t row = (size_t)pos * kv_dim + (size_t)kvh * HD + lane;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                k_wr[row + e] = __float2half_rn(kcur[e]);
-                v_wr[row + e] = __float2half_rn(vcur[e]);
+            for (int i = 0; i < 4; ++i) {
+                k_wr[row + 32 * i] = __float2half_rn(kcur[i]);
+                v_wr[row + 32 * i] = __float2half_rn(vcur[i]);
             }
         }
     }
-    float m[G], l[G], o[G][4];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-        o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
-    }
-    auto load = [&](int t, float (&kf)[4], float (&vf)[4]) {
+    const float inv_sqrt = rsqrt_approx_ftz((float)HD);   // rsqrtf(head_dim), fast-math form
+    // ---- scores of positions [t0, t1): one warp per position
+    for (int t = t0 + warp; t < t1; t += NW) {
+        float kf[4];
         if (fused && t == pos) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                kf[e] = kcur[e];
-                vf[e] = vcur[e];
-            }
-            return;
+            for (int i = 0; i < 4; ++i) kf[i] = kcur[i];
+        } else {
+            ld4(k_cache + (size_t)t * kv_dim + (size_t)kvh * HD, kf);
         }
-        const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
-        const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
-        const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
-        const __half2 k0 = *reinterpret_cast<const __half2*>(&kr.x), k1 = *reinterpret_cast<const __half2*>(&kr.y);
-        const __half2 v0 = *reinterpret_cast<const __half2*>(&vr.x), v1 = *reinterpret_cast<const __half2*>(&vr.y);
-        kf[0] = __low2float(k0);
-        kf[1] = __high2float(k0);
-        kf[2] = __low2float(k1);
-        kf[3] = __high2float(k1);
-        vf[0] = __low2float(v0);
-        vf[1] = __high2float(v0);
-        vf[2] = __low2float(v1);
-        vf[3] = __high2float(v1);
-    };
-    auto consume = [&](const float (&kf)[4], const float (&vf)[4]) {
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            float sdot = qv[g][0] * kf[0];
-            sdot = fmaf(qv[g][1], kf[1], sdot);
-            sdot = fmaf(qv[g][2], kf[2], sdot);
-            sdot = fmaf(qv[g][3], kf[3], sdot);
+            const float a = __fadd_rn(__fmul_rn(qv[g][0], kf[0]), __fmul_rn(qv[g][2], kf[2]));   // strides 64 (d = l, l + 32) ...
+            const float b = __fadd_rn(__fmul_rn(qv[g][1], kf[1]), __fmul_rn(qv[g][3], kf[3]));
+            float c = a + b;                                                                 // ... and 32
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
-            const float sc = sdot * scale;
-            const float mn = fmaxf(m[g], sc);
-            const float corr = __expf(m[g] - mn);   // 0 on the first position (m = -inf)
-            const float pw = __expf(sc - mn);
-            l[g] = l[g] * corr + pw;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
-            m[g] = mn;
-        }
-    };
-    int t = t0 + warp;
-    for (; t + kAttnWarps < t1; t += 2 * kAttnWarps) {
-        float ka[4], va[4], kb[4], vb[4];
-        load(t, ka, va);
-        load(t + kAttnWarps, kb, vb);
-        consume(ka, va);
-        consume(kb, vb);
-    }
-    if (t < t1) {
-        float ka[4], va[4];
-        load(t, ka, va);
-        consume(ka, va);
-    }
-    // merge the 4 warps through shared memory, then this CTA's partial to the workspace
-    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
-    __shared__ float s_o[kAttnWarps][G][HD];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        if (lane == 0) {
-            s_m[warp][g] = m[g];
-            s_l[warp][g] = l[g];
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s_o[warp][g][lane * 4 + e] = o[g][e];
-    }
-    __syncthreads();
-    constexpr int rec = 2 + HD;   // (m, l, o[HD]) per query head
-    float* my = part + ((size_t)kvh * kAttnSplits + split) * G * rec;
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int g = i / HD, d = i % HD;
-        float mm = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
-        float ll = 0.f, oo = 0.f;
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-            const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
-            ll = fmaf(s_l[w][g], f, ll);
-            oo = fmaf(s_o[w][g][d], f, oo);
-        }
-        __stcg(my + g * rec + 2 + d, oo);
-        if (d == 0) {
-            __stcg(my + g * rec, mm);
-            __stcg(my + g * rec + 1, ll);
+            for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+            if (lane == g) __stcg(scores + (size_t)(kvh * G + g) * max_seq + t, c * inv_sqrt);
         }
     }
     __threadfence();
     __syncthreads();
     __shared__ int s_last;
-    if (threadIdx.x == 0) s_last = atomicAdd(counters + kvh, 1) == kAttnSplits - 1;
+    if (threadIdx.x == 0) s_last = atomicAdd(counters + kvh, 1) == kAttnChunks - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    const float* all = part + (size_t)kvh * kAttnSplits * G * rec;
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int g = i / HD, d = i % HD;
-        float ms[kAttnSplits], ls[kAttnSplits], os[kAttnSplits];
+    // ---- the last CTA of this kv head: softmax and P.V, one 128-thread group per query head
+    const int g = threadIdx.x >> 7, d = threadIdx.x & 127, gw = (threadIdx.x >> 5) & 3;
+    float* sc = scores + (size_t)(kvh * G + g) * max_seq;
+    __shared__ float s_max[G][4];
+    __shared__ float s_inv[G];
+    float m = -1e38f;   // the reference's initial value
+    for (int t = d; t < seq; t += 128) m = fmaxf(m, __ldcg(sc + t));
 #pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) {   // independent loads, all in flight
-            const float* r = all + (size_t)sp * G * rec + g * rec;
-            ms[sp] = ldcg_f32(r);
-            ls[sp] = ldcg_f32(r + 1);
-            os[sp] = ldcg_f32(r + 2 + d);
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) s_max[g][gw] = m;
+    named_bar_sync(1 + g, 128);
+    m = fmaxf(fmaxf(s_max[g][0], s_max[g][1]), fmaxf(s_max[g][2], s_max[g][3]));
+    for (int t = d; t < seq; t += 128) __stcg(sc + t, __expf(__ldcg(sc + t) - m));
+    named_bar_sync(1 + g, 128);
+    if (d == 0) {
+        // the denominator in t order: a serial chain; loads run ahead in batches
+        float sum = 0.f;
+        int t = 0;
+        for (; t + 16 <= seq; t += 16) {
+            float e[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) e[i] = __ldcg(sc + t + i);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum += e[i];
         }
-        float mm = -INFINITY;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ms[sp]);
-        float ll = 0.f, oo = 0.f;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) {   // split order: deterministic
-            const float f = ms[sp] == -INFINITY ? 0.f : __expf(ms[sp] - mm);   // empty splits add nothing
-            ll = fmaf(ls[sp], f, ll);
-            oo = fmaf(os[sp], f, oo);
-        }
-        out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
+        for (; t < seq; ++t) sum += __ldcg(sc + t);
+        s_inv[g] = recip_ref(sum);
     }
+    named_bar_sync(1 + g, 128);
+    const float inv = s_inv[g];
+    const __half* vb = v_cache + (size_t)kvh * HD + d;
+    float acc = 0.f;
+    int t = 0;
+    for (; t + 8 <= seq; t += 8) {
+        float e[8], v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            e[i] = __ldcg(sc + t + i);
+            v[i] = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vb) +
+                                                        (size_t)(t + i) * kv_dim)));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc = fmaf(__fmul_rn(e[i], inv), v[i], acc);
+    }
+    for (; t < seq; ++t)
+        acc = fmaf(__fmul_rn(__ldcg(sc + t), inv),
+                   __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vb) + (size_t)t * kv_dim))),
+                   acc);
+    out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(acc);
+    __syncthreads();
     if (threadIdx.x == 0) counters[kvh] = 0;   // leave the workspace counter at zero
 }
 
@@ -323,11 +286,6 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const __half* __restrict__
 }
 
 __global__ void advance_kernel(int* d_pos, int by) { *d_pos += by; }
-
-// Operand order of the RoPE contraction (see rope_pair): form 0 reproduces the
-// reference's rope kernel bit for bit (tests/test_decode_gpu.py pins it; form 1
-// is the other order, kept in rope_pair for that comparison).
-constexpr int kRopeForm = 0;
 
 }  // namespace
 
@@ -367,10 +325,9 @@ extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const flo
 }
 
 
-extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads) {
-    if (n_kv_heads <= 0 || n_heads % n_kv_heads) return 0;
-    const size_t g = n_heads / n_kv_heads;
-    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_kv_heads * kAttnSplits * g * (2 + 128) * 4;
+extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads, int max_seq) {
+    if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_seq <= 0) return 0;
+    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_heads * max_seq * 4;
 }
 
 static af_status attention_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
@@ -381,14 +338,13 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
         n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
         return AF_ERR_INVALID;
     if (head_dim != 128 || n_heads / n_kv_heads > kAttnMaxG) return AF_ERR_UNSUPPORTED;
-    if (!aligned(q, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) || !aligned(out, 2)) return AF_ERR_INVALID;
-    const size_t need = af_decode_attention_workspace_bytes(n_heads, n_kv_heads);
+    if (!aligned(q, 2) || !aligned(k_cache, 2) || !aligned(v_cache, 2) || !aligned(out, 2)) return AF_ERR_INVALID;
+    const size_t need = af_decode_attention_workspace_bytes(n_heads, n_kv_heads, max_seq);
     if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) return AF_ERR_WORKSPACE;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     int* counters = reinterpret_cast<int*>(ws + 256);
-    float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
-    constexpr int warps = 8;
-    const dim3 grid(kAttnSplits, n_kv_heads), block(warps * 32);
+    float* scores = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
+    const dim3 grid(kAttnChunks, n_kv_heads);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
                  *vh = static_cast<const __half*>(v_cache);
@@ -397,10 +353,10 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     __half* kw = cos_tab ? const_cast<__half*>(kh) : nullptr;
     __half* vw = cos_tab ? const_cast<__half*>(vh) : nullptr;
     switch (n_heads / n_kv_heads) {
-#define AF_ATTN(GG) \
-    case GG:                                                                                                  \
-        attention_kernel<GG, warps><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part, counters,    \
-                                                            cos_tab, sin_tab, n_heads, kRopeForm, kw, vw, max_seq); \
+#define AF_ATTN(GG)                                                                                       \
+    case GG:                                                                                              \
+        attention_kernel<GG><<<grid, GG * 128, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, scores, counters, \
+                                                        cos_tab, sin_tab, n_heads, max_seq, kw, vw);      \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN

@@ -1378,18 +1378,6 @@ extern "C" af_status af_w8a16_gemv(const void* x, const void* w, const void* sca
     if (kind != AF_SCALE_NONE && scales == nullptr) return AF_ERR_INVALID;
     if (!aligned(y, 2)) return AF_ERR_INVALID;   // an FP16 output is 2-byte aligned
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (M == 1 && kind == AF_SCALE_GROUP_F16 && chain_ok(x, w, scales, K)) {
-        // the reference's decode GEMV: the chain kernel, bit-identical to it
-        af_chain_op op{};
-        op.kind = AF_OP_GEMV;
-        op.N = N;
-        op.K = K;
-        op.x = x;
-        op.w = w;
-        op.scales = scales;
-        op.y = y;
-        return chain_launch(&op, 1, nullptr, 0, st, true);
-    }
     const int wk = wkind_of(kind);
     for (int m0 = 0; m0 < M; m0 += 16) {
         const int mb = (M - m0 < 16) ? (M - m0) : 16;
@@ -1511,20 +1499,6 @@ extern "C" af_status af_rmsnorm_w8a16_gemv(const void* x, const float* norm_w, f
     if (r != AF_OK) return r;
     if (norm_w == nullptr || !aligned(norm_w, 16) || (x_norm_out != nullptr && !aligned(x_norm_out, 2)))
         return AF_ERR_INVALID;
-    if (kind == AF_SCALE_GROUP_F16 && chain_ok(x, w, scales, K)) {
-        af_chain_op op{};
-        op.kind = AF_OP_RMSNORM_GEMV;
-        op.N = N;
-        op.K = K;
-        op.x = x;
-        op.w = w;
-        op.scales = scales;
-        op.norm_w = norm_w;
-        op.eps = eps;
-        op.y = y;
-        op.xn_out = x_norm_out;
-        return chain_launch(&op, 1, nullptr, 0, static_cast<cudaStream_t>(stream), true);
-    }
     Fused fz;
     fz.norm_w = norm_w;
     fz.eps = eps;
@@ -1538,18 +1512,6 @@ extern "C" af_status af_w8a16_gemv_residual(const void* x, const void* w, const 
     af_status r = fused_checks(x, w, scales, inout, N, K, group_size, kind);
     if (r != AF_OK) return r;
     if (y_out != nullptr && !aligned(y_out, 2)) return AF_ERR_INVALID;
-    if (kind == AF_SCALE_GROUP_F16 && chain_ok(x, w, scales, K)) {
-        af_chain_op op{};
-        op.kind = AF_OP_GEMV_RESIDUAL;
-        op.N = N;
-        op.K = K;
-        op.x = x;
-        op.w = w;
-        op.scales = scales;
-        op.y = inout;
-        op.aux = y_out;
-        return chain_launch(&op, 1, nullptr, 0, static_cast<cudaStream_t>(stream), true);
-    }
     Fused fz;
     fz.res = static_cast<const __half*>(inout);
     fz.aux = static_cast<__half*>(y_out);
@@ -1569,23 +1531,6 @@ extern "C" af_status af_rmsnorm_w8a16_swiglu(const void* x, const float* norm_w,
     if ((gate_up_out != nullptr && !aligned(gate_up_out, 2)) || (x_norm_out != nullptr && !aligned(x_norm_out, 2)))
         return AF_ERR_INVALID;
     if (norm_w == nullptr && x_norm_out != nullptr) return AF_ERR_INVALID;
-    if (norm_w != nullptr && chain_ok(x, w_gate, s_gate, K) && chain_ok(x, w_up, s_up, K)) {
-        af_chain_op op{};
-        op.kind = AF_OP_RMSNORM_SWIGLU;
-        op.N = N;
-        op.K = K;
-        op.x = x;
-        op.w = w_gate;
-        op.scales = s_gate;
-        op.w2 = w_up;
-        op.scales2 = s_up;
-        op.norm_w = norm_w;
-        op.eps = eps;
-        op.y = h;
-        op.xn_out = x_norm_out;
-        op.aux = gate_up_out;
-        return chain_launch(&op, 1, nullptr, 0, static_cast<cudaStream_t>(stream), true);
-    }
     Fused fz;
     fz.norm_w = norm_w;
     fz.eps = eps;

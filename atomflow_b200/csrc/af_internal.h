@@ -34,7 +34,7 @@ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // call (shallower ring, two CTAs per SM, programmatic dependent launch).
 constexpr int kChainMaxK = 16384;
 af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_t ws_bytes, cudaStream_t st,
-                       bool single);
+                       bool single, bool exact);
 inline bool chain_ok(const void* x, const void* w, const void* s, int K) {
     return K > 0 && K % 128 == 0 && K <= kChainMaxK && x != nullptr && w != nullptr && s != nullptr &&
            aligned(x, 16) && aligned(w, 16) && aligned(s, 2);

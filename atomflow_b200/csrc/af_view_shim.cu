@@ -109,6 +109,22 @@ void launch_w8a16_gemv(const View& act_x, const View& weight, const View& scales
         report(AF_ERR_INVALID, "launch_w8a16_gemv");
         return;
     }
+    if (M == 1 && group_size == 128 && af::chain_ok(act_x.data_ptr, weight.data_ptr, scales.data_ptr, K) &&
+        af::aligned(output.data_ptr, 2)) {
+        // the reference's decode GEMV: the exact chain kernel, bit-identical to
+        // w8a16_gemv_kernel, so an engine linked against this library produces
+        // the unmodified build's outputs
+        af_chain_op op{};
+        op.kind = AF_OP_GEMV;
+        op.N = N;
+        op.K = K;
+        op.x = act_x.data_ptr;
+        op.w = weight.data_ptr;
+        op.scales = scales.data_ptr;
+        op.y = output.data_ptr;
+        report(af::chain_launch(&op, 1, nullptr, 0, stream, true, true), "launch_w8a16_gemv");
+        return;
+    }
     void* ws = nullptr;
     af_status st = workspace_for(af_w8a16_gemv_workspace_bytes(M, N, K, AF_SCALE_GROUP_F16),
                                  stream, &ws);

@@ -82,7 +82,7 @@ class DecodeEngine:
         self.logits = z(self.V, torch.float32)
         self.d_token = z(1, torch.int32)
         self.d_pos = z(1, torch.int32)
-        aw = self.L.af_decode_attention_workspace_bytes(self.NH, self.NKV)
+        aw = self.L.af_decode_attention_workspace_bytes(self.NH, self.NKV, max_seq_len)
         self.attn_ws = z(aw, torch.uint8)
         lw = self.L.af_lm_head_workspace_bytes(self.V, self.D, 0)
         self.lm_ws = z(lw, torch.uint8)

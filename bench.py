@@ -201,10 +201,11 @@ class OursChain:
     N > 1 the row-split O/down are af_w8a16_gemv_allreduce_residual."""
     launches_per_layer = 4
 
-    def __init__(self, bufs, as_chain=False):
+    def __init__(self, bufs, as_chain=False, exact=False):
         self.L = af_lib()
         self.b = bufs
         self.comm = None
+        self.fn = self.L.af_gemv_chain if exact else self.L.af_gemv_chain_fast
         if as_chain:
             from atomflow_b200._lib import ChainOp
             self.ChainOp = ChainOp
@@ -228,8 +229,7 @@ class OursChain:
                     C(kind=1, N=dn["N"], K=dn["K"], wait_prev=1, x=p(b["h"]), w=p(dn["q"]), scales=p(dn["s"]),
                       y=p(b["x"]))]
         arr = (C * len(ops))(*ops)
-        self._check(self.L.af_gemv_chain(arr, len(ops), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream),
-                    "af_gemv_chain")
+        self._check(self.fn(arr, len(ops), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream), "af_gemv_chain")
 
     def _check(self, rc, what):
         if rc != 0:
@@ -369,10 +369,11 @@ class OursChainSet:
     next GEMV's weights stream in."""
     launches_per_item = 1 / 140
 
-    def __init__(self, items, device, wait=True):
+    def __init__(self, items, device, wait=True, exact=False):
         from atomflow_b200._lib import ChainOp
         self.L = af_lib()
         self.wait = wait
+        self.fn = self.L.af_gemv_chain if exact else self.L.af_gemv_chain_fast
         self.ChainOp = ChainOp
         self.ws = torch.zeros(self.L.af_chain_workspace_bytes(len(items)), dtype=torch.uint8, device=device)
 
@@ -385,7 +386,7 @@ class OursChainSet:
 
     def launch_all(self, stream, items, xptrs=None, yptrs=None):
         ops = self.ops(items, xptrs, yptrs)
-        rc = self.L.af_gemv_chain(ops, len(items), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream)
+        rc = self.fn(ops, len(items), self.ws.data_ptr(), self.ws.numel(), stream.cuda_stream)
         if rc != 0:
             raise RuntimeError(f"af_gemv_chain: {self.L.af_status_string(rc).decode()}")
 
@@ -693,7 +694,9 @@ def main():
     ap.add_argument("--workload", default="layerset")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--launch", choices=["chain", "per-gemv"], default="chain",
+    ap.add_argument("--math", choices=["fast", "exact"], default="fast",
+                    help="chain: tensor-core dot products (fast) or the reference kernel's FP32 FMA order (exact)")
+    ap.add_argument("--launch", choices=["chain", "per-gemv"], default="per-gemv",
                     help="one-token GEMVs on one GPU: one persistent launch per step (chain) or one launch per GEMV")
     ap.add_argument("--no-token-check", action="store_true",
                     help="decode: skip comparing 64 greedy tokens with the reference engine")
@@ -769,10 +772,15 @@ def main():
     # one token per GEMV on one GPU: the whole step as one persistent launch (af_gemv_chain)
     use_chain = (args.impl == "ours" and tp == 1 and not lm and args.launch == "chain" and
                  all(it["x"].shape[0] == 1 for it in items if not chain))
+    exact = args.math == "exact"
+    if use_chain:
+        config["launch"] = "one persistent launch per step, every GEMV waits for the previous one"
+        config["math"] = ("exact: the reference kernel's FP32 FMA order, bit-identical" if exact else
+                          "fast: tensor-core MMAs, FP32 accumulation, within FP16 rounding of FP64")
     if chain:
-        arm = OursChain(cbufs, as_chain=use_chain) if args.impl == "ours" else None
+        arm = OursChain(cbufs, as_chain=use_chain, exact=exact) if args.impl == "ours" else None
     elif use_chain:
-        arm = OursChainSet(items, device)
+        arm = OursChainSet(items, device, exact=exact)
     else:
         arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
     if args.impl == "reference":
@@ -906,7 +914,7 @@ def main():
                      "traffic": traffic_from_profiles(wl, len(items)) if args.impl == "ours" else None,
                      "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
                                  "reference": "cublasGemmEx + argmax (reference)"} if lm else
-                                {"ours": "chain_kernel (af_gemv_chain, one persistent launch per step)" if use_chain
+                                {"ours": f"chain_kernel<{'exact' if exact else 'fast'}> (one persistent launch per step)" if use_chain
                                  else "chain_kernel / gemv_fp8_m1_kernel (one launch per GEMV)",
                                  "reference": "w8a16_gemv_kernel (reference)"})[args.impl],
                      "per_launch": f"{step_bytes / (launches / args.steps) / 1e6:.2f} MB avg algorithmic bytes / launch "

@@ -83,9 +83,9 @@ af_status af_workspace_reset(void* workspace, size_t workspace_bytes, void* stre
  *   y : FP16 [M, N] row-major          scales: see af_scale_kind
  * FP32 accumulation, FP16 round-to-nearest output.  M = 1 is the decode
  * case of the reference; 1 <= M <= 16 runs in one pass over W, larger M in
- * ceil(M/16) passes.  M = 1 with group scales (the reference's decode GEMV)
- * runs the chain kernel (af_gemv_chain) and is bit-identical to the
- * reference's w8a16_gemv_kernel.  Returns AF_ERR_INVALID for group_size != 128 with
+ * ceil(M/16) passes (tensor-core math, within FP16 rounding of FP64; the
+ * bit-identical form of the reference kernel is af_gemv_chain, and the View
+ * launcher launch_w8a16_gemv uses it).  Returns AF_ERR_INVALID for group_size != 128 with
  * AF_SCALE_GROUP_F16, or K % 128 != 0 with group scales (the reference kernel
  * hard-codes 128-wide groups, qkv_gemm.cu:70). */
 size_t af_w8a16_gemv_workspace_bytes(int M, int N, int K, af_scale_kind kind);
@@ -200,10 +200,12 @@ af_status af_w8a16_gemv_allreduce_residual(const void* x, const void* w, const v
  *   af_rope_kv_write     rotate q and k in qkv at *d_pos, write k and v to row
  *                        *d_pos of the caches (rope.cu; helpers.cu k_write_kv_cache)
  *   af_decode_attention  softmax(q k^T / sqrt(HD)) v over positions 0..*d_pos,
- *                        GQA (NH % NKV == 0, NH/NKV <= 8), HD = 128; split over
- *                        the cache, deterministic merge.  Workspace: zeroed once
- *                        (af_workspace_reset), one per stream; every call leaves
- *                        it zeroed.  (tiled_attention.cu gqa_cached_attention_kernel)
+ *                        GQA (NH % NKV == 0, NH/NKV <= 8), HD = 128; bit-identical
+ *                        to the reference's gqa_cached_attention_kernel
+ *                        (tiled_attention.cu:196-269).  Workspace:
+ *                        af_decode_attention_workspace_bytes(NH, NKV, max_seq),
+ *                        zeroed once (af_workspace_reset), one per stream; every
+ *                        call leaves its counters at zero.
  *   af_rmsnorm           the reference's rms_norm arithmetic, one vector
  *   af_decode_advance    *d_pos += by (the step's last launch)
  * max_seq is the caches' and tables' row count: a kernel that reads *d_pos
@@ -214,7 +216,7 @@ af_status af_embed_lookup(const float* table, const int* d_token, void* x, int D
 af_status af_rope_tables(float* cos_out, float* sin_out, int max_seq, int head_dim, float base);
 af_status af_rope_kv_write(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos, void* k_cache,
                            void* v_cache, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* stream);
-size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads);
+size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads, int max_seq);
 af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos, void* out,
                               int n_heads, int n_kv_heads, int head_dim, int max_seq, void* workspace,
                               size_t workspace_bytes, void* stream);
@@ -278,6 +280,13 @@ typedef struct af_chain_op {
 } af_chain_op;
 size_t af_chain_workspace_bytes(int n_ops);
 af_status af_gemv_chain(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes, void* stream);
+/* The same chain with the dot products on the tensor cores (FP8 -> FP16
+ * packed conversion, m16n8k16 MMAs, FP32 accumulation, the group scale applied
+ * to each 128-position group sum): deterministic, every output within 2 FP16
+ * ulp / 2e-3 relative of FP64 (the reference kernel's own tolerance), but not
+ * its summation order, so not bit-identical to it.  Same arguments. */
+af_status af_gemv_chain_fast(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
+                             void* stream);
 
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for

@@ -49,7 +49,8 @@ struct View {
 
 /* include/ops/kernel.h:138-145 -- W8A16 GEMV.  act_x FP16 [M, K] (M from the
  * leading dims, as calculate_rows, kernel.h:11-18), weight FP8 [N, K], scales
- * FP16 [N, K/group_size], output FP16 [M, N]. */
+ * FP16 [N, K/group_size], output FP16 [M, N].  One token (the reference's
+ * case) is bit-identical to the reference's w8a16_gemv_kernel. */
 void launch_w8a16_gemv(const View& act_x, const View& weight, const View& scales,
                        View& output, int group_size, cudaStream_t stream);
 

@@ -60,8 +60,10 @@ def test_gemv_bit_identical_to_reference_kernel(N, K):
     xd, qd, sd = dev(x), dev(q), dev(s)
     ours = torch.zeros(N, dtype=torch.int16, device="cuda")
     theirs = torch.zeros(N, dtype=torch.int16, device="cuda")
-    assert L().af_w8a16_gemv(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), ours.data_ptr(), 1, N, K, 128, 0,
-                             None, 0, st()) == 0
+    from atomflow_b200._lib import ChainOp, OpKind
+    op = ChainOp(kind=OpKind.GEMV, N=N, K=K, x=xd.data_ptr(), w=qd.data_ptr(), scales=sd.data_ptr(),
+                 y=ours.data_ptr())
+    assert L().af_gemv_chain(ctypes.byref(op), 1, None, 0, st()) == 0
     assert R().afref_w8a16_gemv(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), theirs.data_ptr(), N, K, st()) == 0
     torch.cuda.synchronize()
     a, b = ours.cpu().numpy(), theirs.cpu().numpy()
@@ -184,7 +186,7 @@ def test_chain_repeat_and_graph_replay():
 
 
 def test_chain_independent_ops_match_single_calls():
-    """A layer-set chain (independent x per op, no waits) equals one call per op."""
+    """A layer-set chain (independent x per op, no waits) equals one launch per op."""
     from atomflow_b200._lib import ChainOp, OpKind
     g = torch.Generator(device="cuda")
     g.manual_seed(3)
@@ -199,8 +201,9 @@ def test_chain_independent_ops_match_single_calls():
                                    for (N, K, q, s, x, y, _) in items])
     assert L().af_gemv_chain(ops, len(items), None, 0, st()) == 0
     for (N, K, q, s, x, _, y1) in items:
-        assert L().af_w8a16_gemv(x.data_ptr(), q.data_ptr(), s.data_ptr(), y1.data_ptr(), 1, N, K, 128, 0, None, 0,
-                                 st()) == 0
+        one = ChainOp(kind=OpKind.GEMV, N=N, K=K, x=x.data_ptr(), w=q.data_ptr(), scales=s.data_ptr(),
+                      y=y1.data_ptr())
+        assert L().af_gemv_chain(ctypes.byref(one), 1, None, 0, st()) == 0
     torch.cuda.synchronize()
     for (N, K, q, s, x, y, y1) in items:
         assert torch.equal(y.view(torch.int16), y1.view(torch.int16)), (N, K)
@@ -223,3 +226,48 @@ def test_chain_rejects_bad_arguments():
     assert L().af_gemv_chain(two, 2, None, 0, st()) == 5       # waits need the workspace
     assert L().af_gemv_chain(two, 0, None, 0, st()) == 1
     torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------- fast path
+
+@pytest.mark.parametrize("N,K", [(3072, 3072), (5120, 3072), (8192, 3072), (3072, 8192), (4096, 14336), (1, 128),
+                                 (17, 256), (77, 640), (1000, 1536), (4099, 512), (300, 16384)])
+def test_fast_chain_gemv_within_tolerance(N, K):
+    from atomflow_b200._lib import ChainOp, OpKind
+    from tests._util import assert_fp16_parity
+    x, q, s = make_gemv_case(N * 3 + K, 1, N, K)
+    xd, qd, sd = dev(x), dev(q), dev(s)
+    y = torch.zeros(N, dtype=torch.int16, device="cuda")
+    op = ChainOp(kind=OpKind.GEMV, N=N, K=K, x=xd.data_ptr(), w=qd.data_ptr(), scales=sd.data_ptr(), y=y.data_ptr())
+    assert L().af_gemv_chain_fast(ctypes.byref(op), 1, None, 0, st()) == 0
+    torch.cuda.synchronize()
+    yb = y.cpu().numpy().view(np.uint16)
+    assert_fp16_parity(yb, oracle.gemv_f64(x, q, s, "group", with_l2=True), f"fast {N}x{K}",
+                       oracle.gemv_refmath(x, q, s, 8) if N * K <= 4_000_000 else None)
+    # deterministic
+    y2 = torch.zeros_like(y)
+    op.y = y2.data_ptr()
+    assert L().af_gemv_chain_fast(ctypes.byref(op), 1, None, 0, st()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+
+
+def test_fast_layer_chain_matches_exact_within_rounding():
+    """The tensor-core chain and the exact chain on the same 3 decode layers: the
+    residual stream agrees to FP16 rounding (each op's error is within the GEMV
+    tolerance; through 12 ops they compound only to a few FP16 ulp)."""
+    layers, x0 = _layers(3, seed=13)
+    fast, exact = _bufs(), _bufs()
+    fast["x"].copy_(x0)
+    exact["x"].copy_(x0)
+    ops_f, n = _chain_ops(layers, fast)
+    ops_e, _ = _chain_ops(layers, exact)
+    ws = torch.zeros(L().af_chain_workspace_bytes(n), dtype=torch.uint8, device="cuda")
+    assert L().af_gemv_chain_fast(ops_f, n, ws.data_ptr(), ws.numel(), st()) == 0
+    assert L().af_gemv_chain(ops_e, n, ws.data_ptr(), ws.numel(), st()) == 0
+    torch.cuda.synchronize()
+    a, b = fast["x"].float(), exact["x"].float()
+    rms = float(b.pow(2).mean().sqrt())
+    err = (a - b).abs()
+    assert float(err.max()) <= 1e-2 * rms + 4 * 2.0 ** -10 * float(b.abs().max()), (float(err.max()), rms)
+    assert int(ws.count_nonzero()) == 0

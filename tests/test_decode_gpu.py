@@ -129,7 +129,7 @@ def test_decode_attention_parity():
     g.manual_seed(11)
     kc = torch.randn(MAXSEQ, NKV * HD, generator=g, device="cuda").half()
     vc = torch.randn(MAXSEQ, NKV * HD, generator=g, device="cuda").half()
-    ws = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV, MAXSEQ), dtype=torch.uint8, device="cuda")
     for pos in (0, 1, 7, 31, 100, 1024, 2047):
         q = (torch.randn(NH * HD, generator=g, device="cuda") * 2).half()
         dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
@@ -144,6 +144,9 @@ def test_decode_attention_parity():
                                             NH, NKV, st()) == 0
         torch.cuda.synchronize()
         assert torch.equal(outs[0], outs[1])
+        # bit for bit the reference kernel's output
+        nbad = int((outs[0].view(torch.int16) != o_ref.view(torch.int16)).sum())
+        assert nbad == 0, f"pos {pos}: {nbad} of {NH * HD} outputs differ from the reference attention kernel"
         want = _attention_f64(q, kc, vc, pos + 1)
         for name, got in (("ours", outs[0]), ("reference", o_ref)):
             y = got.float().cpu().numpy().astype(np.float64)
@@ -158,7 +161,7 @@ def test_fused_rope_attention_equals_the_two_kernels():
     g = torch.Generator(device="cuda")
     g.manual_seed(17)
     qd, kvd = NH * HD, NKV * HD
-    ws_a = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV), dtype=torch.uint8, device="cuda")
+    ws_a = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV, MAXSEQ), dtype=torch.uint8, device="cuda")
     ws_b = torch.zeros_like(ws_a)
     kc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
     vc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
@@ -193,7 +196,7 @@ def test_position_outside_the_cache_is_skipped_and_flagged():
     qd, kvd = NH * HD, NKV * HD
     flt = ctypes.c_uint(0)
     assert L.af_device_faults(ctypes.byref(flt), 1) == 0
-    ws = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(L.af_decode_attention_workspace_bytes(NH, NKV, MAXSEQ), dtype=torch.uint8, device="cuda")
     qkv = torch.randn(qd + 2 * kvd, device="cuda").half()
     small = 64   # caches with 64 rows; the buffers run on past them, so a stray write would show
     kc = torch.zeros(2 * small, kvd, dtype=torch.float16, device="cuda")

@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(G * 128) attention_kernel(
     const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
     const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ scores,
     int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
-    int max_seq, __half* k_wr, __half* v_wr) {
+    int max_seq, int head_dim, __half* k_wr, __half* v_wr) {
     // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
     // vector: every CTA rotates its own query heads (rounded to FP16, as the
     // reference stores them), the current position's k (rotated) and v come
@@ -179,7 +179,10 @@ __global__ void __launch_bounds__(G * 128) attention_kernel(
             }
         }
     }
-    const float inv_sqrt = rsqrt_approx_ftz((float)HD);   // rsqrtf(head_dim), fast-math form
+    // rsqrtf of the runtime head dim, as the reference computes it
+    // (tiled_attention.cu:211); this file is built with --use_fast_math like the
+    // reference, which is what makes the value and its use round identically
+    const float inv_sqrt = rsqrtf(static_cast<float>(head_dim));
     // ---- scores of positions [t0, t1): one warp per position
     for (int t = t0 + warp; t < t1; t += NW) {
         float kf[4];
@@ -356,7 +359,7 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
 #define AF_ATTN(GG)                                                                                       \
     case GG:                                                                                              \
         attention_kernel<GG><<<grid, GG * 128, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, scores, counters, \
-                                                        cos_tab, sin_tab, n_heads, max_seq, kw, vw);      \
+                                                        cos_tab, sin_tab, n_heads, max_seq, head_dim, kw, vw);      \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN

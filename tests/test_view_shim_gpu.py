@@ -31,7 +31,7 @@ def test_launch_w8a16_gemv_view():
     assert L.af_view_last_status() == 0
     assert_fp16_parity(yd.cpu().numpy().view(np.uint16), oracle.gemv_f64(x, q, s, "group", with_l2=True), "view")
     # the drop-in is bit-identical to the reference kernel
-    np.testing.assert_array_equal(yd.cpu().numpy().view(np.uint16), oracle.gemv_refmath(x, q, s, 8))
+    np.testing.assert_array_equal(yd.cpu().numpy().view(np.uint16).reshape(-1), oracle.gemv_refmath(x, q, s, 8).reshape(-1))
     # a wrong dtype is rejected, recorded, and launches nothing
     vbad = make_view(qd.data_ptr(), DataType.FP16, [N, K])
     L.launch_w8a16_gemv(ctypes.byref(vx), ctypes.byref(vbad), ctypes.byref(vs), ctypes.byref(vy), 128, st)

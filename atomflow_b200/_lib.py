@@ -97,11 +97,27 @@ C_SYMBOLS = {
     "af_decode_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "af_decode_rope_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "af_device_faults": (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    "af_decode_rope_attention_fast": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "af_rmsnorm": (_i, [_vp, _vp, ctypes.c_float, _vp, _i, _vp]),
     "af_decode_advance": (_i, [_vp, _i, _vp]),
     "af_chain_workspace_bytes": (_sz, [_i]),
     "af_gemv_chain": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
     "af_gemv_chain_fast": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
+    "af_engine_create": (_i, [ctypes.c_char_p, _i, _i, _i, ctypes.POINTER(ctypes.c_void_p)]),
+    "af_engine_destroy": (_i, [_vp]),
+    "af_engine_info": (_i, [_vp, ctypes.POINTER(ctypes.c_int)]),
+    "af_engine_set_position": (_i, [_vp, _i]),
+    "af_engine_get_position": (_i, [_vp, ctypes.POINTER(ctypes.c_int)]),
+    "af_engine_inject_token": (_i, [_vp, _i]),
+    "af_engine_output_token": (_i, [_vp, ctypes.POINTER(ctypes.c_int)]),
+    "af_engine_step": (_i, [_vp, _i]),
+    "af_engine_capture": (_i, [_vp, _i]),
+    "af_engine_replay": (_i, [_vp, _i]),
+    "af_engine_synchronize": (_i, [_vp]),
+    "af_engine_stream": (_vp, [_vp]),
+    "af_engine_device_token": (_vp, [_vp]),
+    "af_engine_device_position": (_vp, [_vp]),
+    "af_engine_logits": (_vp, [_vp]),
     "af_view_last_status": (_i, []),
     "af_view_set_argmax_mode": (_i, [_i]),
 }

@@ -15,6 +15,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libatomflow_b200.so"
+CLI = PKG / "af_generate"        # the C++ greedy-decode driver on the C ABI
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-cudart", "shared"]
 
@@ -24,11 +25,12 @@ def sources():
 
 
 def headers():
-    return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
+    return (sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.cpp")) +
+            sorted((ROOT / "include").glob("*.h")))
 
 
 def up_to_date() -> bool:
-    if not LIB.exists():
+    if not LIB.exists() or not CLI.exists():
         return False
     t = LIB.stat().st_mtime
     return all(p.stat().st_mtime <= t for p in sources() + headers())
@@ -61,6 +63,12 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True, cwd=str(PKG))
     os.replace(tmp, LIB)
+    cmd = [nvcc, *ARCH, "-O2", "-std=c++17", "-I", str(ROOT / "include"), "-o", str(CLI),
+           str(CSRC / "af_generate.cpp"), "-L", str(PKG), "-latomflow_b200", "-cudart", "shared",
+           "-Xlinker", "-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True, cwd=str(PKG))
     return LIB
 
 

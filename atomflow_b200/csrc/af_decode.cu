@@ -101,6 +101,14 @@ __global__ void rope_kv_kernel(__half* __restrict__ qkv, const float* __restrict
 // 128-thread group per query head, reading the scores back from the workspace.
 constexpr int kAttnChunks = 16;
 constexpr int kAttnMaxG = 8;
+constexpr int kVChunk = 64;   // V rows per shared-memory window of the P.V phase
+constexpr int kVBufs = 4;     // windows in flight: V streams kVBufs - 1 windows ahead of the FMA chains
+constexpr size_t kAttnSmemMax = 200 * 1024;
+
+// Dynamic shared memory of attention_kernel<G>: the G heads' scores and two V windows.
+inline size_t attn_smem(int G, int max_seq) {
+    return (size_t)G * max_seq * 4 + (size_t)kVBufs * kVChunk * 128 * 2;
+}
 
 // Operand order of the RoPE contraction (see rope_pair): form 0 reproduces the
 // reference's rope kernel bit for bit (tests/test_decode_gpu.py pins it; form 1
@@ -112,6 +120,16 @@ constexpr int kRecipForm = 0;
 
 __device__ __forceinline__ float recip_ref(float x) {
     return kRecipForm == 0 ? rcp_approx_ftz(x) : fdiv_full_ftz(1.0f, x);
+}
+
+// (a0, a1) = (fma(p, v0, a0), fma(p, v1, a1)) in one packed FP32 FMA.
+__device__ __forceinline__ void fma2(float& a0, float& a1, float p, float v0, float v1) {
+    unsigned long long av, pv, vv;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(av) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1,%1};" : "=l"(pv) : "f"(p));
+    asm("mov.b64 %0, {%1,%2};" : "=l"(vv) : "f"(v0), "f"(v1));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(av) : "l"(pv), "l"(vv));
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(a0), "=f"(a1) : "l"(av));
 }
 
 template <int G>
@@ -183,23 +201,33 @@ __global__ void __launch_bounds__(G * 128) attention_kernel(
     // (tiled_attention.cu:211); this file is built with --use_fast_math like the
     // reference, which is what makes the value and its use round identically
     const float inv_sqrt = rsqrtf(static_cast<float>(head_dim));
-    // ---- scores of positions [t0, t1): one warp per position
-    for (int t = t0 + warp; t < t1; t += NW) {
-        float kf[4];
-        if (fused && t == pos) {
+    // ---- scores of positions [t0, t1): one warp per position, four positions'
+    // keys loaded before any is reduced (the loads overlap)
+    constexpr int kU = 4;
+    for (int tb = t0 + warp * kU; tb < t1; tb += NW * kU) {
+        float kf[kU][4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) kf[i] = kcur[i];
-        } else {
-            ld4(k_cache + (size_t)t * kv_dim + (size_t)kvh * HD, kf);
+        for (int u = 0; u < kU; ++u) {
+            const int t = tb + u;
+            if (t < t1 && !(fused && t == pos)) ld4(k_cache + (size_t)t * kv_dim + (size_t)kvh * HD, kf[u]);
+            else
+#pragma unroll
+                for (int i = 0; i < 4; ++i) kf[u][i] = kcur[i];
         }
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float a = __fadd_rn(__fmul_rn(qv[g][0], kf[0]), __fmul_rn(qv[g][2], kf[2]));   // strides 64 (d = l, l + 32) ...
-            const float b = __fadd_rn(__fmul_rn(qv[g][1], kf[1]), __fmul_rn(qv[g][3], kf[3]));
-            float c = a + b;                                                                 // ... and 32
+        for (int u = 0; u < kU; ++u) {
+            const int t = tb + u;
+            if (t >= t1) break;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
-            if (lane == g) __stcg(scores + (size_t)(kvh * G + g) * max_seq + t, c * inv_sqrt);
+            for (int g = 0; g < G; ++g) {
+                // strides 64 (dims l and l + 32) and 32 in-lane, then 16 .. 1 across lanes
+                const float a = __fadd_rn(__fmul_rn(qv[g][0], kf[u][0]), __fmul_rn(qv[g][2], kf[u][2]));
+                const float b = __fadd_rn(__fmul_rn(qv[g][1], kf[u][1]), __fmul_rn(qv[g][3], kf[u][3]));
+                float c = a + b;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+                if (lane == g) __stcg(scores + (size_t)(kvh * G + g) * max_seq + t, c * inv_sqrt);
+            }
         }
     }
     __threadfence();
@@ -209,58 +237,341 @@ __global__ void __launch_bounds__(G * 128) attention_kernel(
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // ---- the last CTA of this kv head: softmax and P.V, one 128-thread group per query head
+    // ---- the last CTA of this kv head: softmax and P.V, one 128-thread group per
+    // query head, on the scores copied into shared memory; V streams through a
+    // double-buffered shared-memory window of kVChunk positions (cp.async)
+    constexpr int NT = G * 128;
+    extern __shared__ __align__(16) float dsm[];
+    float* es = dsm;                                                   // [G][max_seq]
+    __half* vbuf = reinterpret_cast<__half*>(dsm + (size_t)G * max_seq);  // [kVBufs][kVChunk][HD]
     const int g = threadIdx.x >> 7, d = threadIdx.x & 127, gw = (threadIdx.x >> 5) & 3;
-    float* sc = scores + (size_t)(kvh * G + g) * max_seq;
+    const unsigned char* vsrc = reinterpret_cast<const unsigned char*>(v_cache + (size_t)kvh * HD);
+    const int nch = (seq + kVChunk - 1) / kVChunk;
+    auto issue_v = [&](int c) {   // rows [c*kVChunk, ...) of this kv head's V: 256 bytes each, 16 per thread-copy
+        unsigned char* dst = reinterpret_cast<unsigned char*>(vbuf + (size_t)(c % kVBufs) * kVChunk * HD);
+        const int r0 = c * kVChunk, nr = min(kVChunk, seq - r0);
+        for (int i = threadIdx.x; i < nr * 16; i += NT) {
+            const int r = i >> 4, piece = i & 15;
+            cp_async16(smem_u32(dst + r * 256 + piece * 16), vsrc + (size_t)(r0 + r) * kv_dim * 2 + piece * 16);
+        }
+        cp_async_commit();
+    };
+    // the first windows of V load while the softmax runs (an empty commit group
+    // past the end keeps the group count uniform)
+    for (int c = 0; c < kVBufs - 1; ++c) {
+        if (c < nch) issue_v(c);
+        else cp_async_commit();
+    }
+    for (int gg = 0; gg < G; ++gg)
+        for (int t = threadIdx.x; t < seq; t += NT) es[gg * max_seq + t] = __ldcg(scores + (size_t)(kvh * G + gg) * max_seq + t);
+    __syncthreads();
+    float* e = es + (size_t)g * max_seq;
     __shared__ float s_max[G][4];
     __shared__ float s_inv[G];
     float m = -1e38f;   // the reference's initial value
-    for (int t = d; t < seq; t += 128) m = fmaxf(m, __ldcg(sc + t));
+    for (int t = d; t < seq; t += 128) m = fmaxf(m, e[t]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if (lane == 0) s_max[g][gw] = m;
     named_bar_sync(1 + g, 128);
     m = fmaxf(fmaxf(s_max[g][0], s_max[g][1]), fmaxf(s_max[g][2], s_max[g][3]));
-    for (int t = d; t < seq; t += 128) __stcg(sc + t, __expf(__ldcg(sc + t) - m));
+    for (int t = d; t < seq; t += 128) e[t] = __expf(e[t] - m);
     named_bar_sync(1 + g, 128);
     if (d == 0) {
-        // the denominator in t order: a serial chain; loads run ahead in batches
+        // the denominator in t order: a serial chain over shared memory
         float sum = 0.f;
         int t = 0;
-        for (; t + 16 <= seq; t += 16) {
-            float e[16];
+        for (; t + 32 <= seq; t += 32) {
+            float v32[32];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) e[i] = __ldcg(sc + t + i);
+            for (int i = 0; i < 32; ++i) v32[i] = e[t + i];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sum += e[i];
+            for (int i = 0; i < 32; ++i) sum += v32[i];
         }
-        for (; t < seq; ++t) sum += __ldcg(sc + t);
+        for (; t < seq; ++t) sum += e[t];
         s_inv[g] = recip_ref(sum);
     }
-    named_bar_sync(1 + g, 128);
-    const float inv = s_inv[g];
-    const __half* vb = v_cache + (size_t)kvh * HD + d;
-    float acc = 0.f;
-    int t = 0;
-    for (; t + 8 <= seq; t += 8) {
-        float e[8], v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            e[i] = __ldcg(sc + t + i);
-            v[i] = __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vb) +
-                                                        (size_t)(t + i) * kv_dim)));
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc = fmaf(__fmul_rn(e[i], inv), v[i], acc);
+    __syncthreads();
+    // p[t] = e[t] * (1 / sum), the reference's normalised scores, once per head
+    {
+        const float inv = s_inv[g];
+        for (int t = d; t < seq; t += 128) e[t] = __fmul_rn(e[t], inv);
     }
-    for (; t < seq; ++t)
-        acc = fmaf(__fmul_rn(__ldcg(sc + t), inv),
-                   __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vb) + (size_t)t * kv_dim))),
-                   acc);
-    out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(acc);
+    __syncthreads();
+    // out[d] = sum_t p[t] * v[t][d], an FMA chain in t order per dim; a thread
+    // runs two dims' chains in one packed FMA (two independent FMAs)
+    const bool pv_lane = d < 64;
+    float acc0 = 0.f, acc1 = 0.f;
+    for (int c = 0; c < nch; ++c) {
+        // window c + kVBufs - 1 reuses the buffer of window c - 1: every thread is past it
+        if (c + kVBufs - 1 < nch) issue_v(c + kVBufs - 1);
+        else cp_async_commit();
+        cp_async_wait<kVBufs - 1>();   // window c has landed
+        __syncthreads();
+        if (pv_lane) {
+            const __half2* vb = reinterpret_cast<const __half2*>(vbuf + (size_t)(c % kVBufs) * kVChunk * HD) + d;
+            const float* pc = e + c * kVChunk;
+            const int nr = min(kVChunk, seq - c * kVChunk);
+            if (nr == kVChunk) {
+                // software-pipelined: batch b + 1's loads are in flight while batch b accumulates
+                constexpr int B = 8;
+                float pa[B], pb[B];
+                __half2 va[B], vbb[B];
+#pragma unroll
+                for (int k = 0; k < B; ++k) {
+                    pa[k] = pc[k];
+                    va[k] = vb[k * (HD / 2)];
+                }
+#pragma unroll
+                for (int i = 0; i < kVChunk; i += B) {
+                    if (i + B < kVChunk) {
+#pragma unroll
+                        for (int k = 0; k < B; ++k) {
+                            pb[k] = pc[i + B + k];
+                            vbb[k] = vb[(i + B + k) * (HD / 2)];
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < B; ++k) {
+                        const float2 vf = __half22float2(va[k]);
+                        fma2(acc0, acc1, pa[k], vf.x, vf.y);
+                    }
+#pragma unroll
+                    for (int k = 0; k < B; ++k) {
+                        pa[k] = pb[k];
+                        va[k] = vbb[k];
+                    }
+                }
+            } else {
+                for (int i = 0; i < nr; ++i) {
+                    const float2 vf = __half22float2(vb[i * (HD / 2)]);
+                    fma2(acc0, acc1, pc[i], vf.x, vf.y);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (pv_lane) {
+        out[(size_t)(kvh * G + g) * HD + 2 * d] = __float2half_rn(acc0);
+        out[(size_t)(kvh * G + g) * HD + 2 * d + 1] = __float2half_rn(acc1);
+    }
     __syncthreads();
     if (threadIdx.x == 0) counters[kvh] = 0;   // leave the workspace counter at zero
 }
+
+// ------------------------------------------- cached attention, fast form
+// Split-KV GQA attention for one token, within FP16 rounding of FP64 (online
+// softmax: not the reference's summation order, so not bit-identical to it).  CTA (split, kv head) handles
+// positions [t0, t1) of the cache for the G = NH/NKV query heads that share
+// the kv head; each of its 8 warps takes every 8th position with an online
+// softmax (lane l holds dims 4l..4l+3; two positions' loads in flight).  The
+// CTA's partial (max, sum, o) goes to the workspace; the last CTA of the kv
+// head merges the splits in split order (deterministic) and writes out, then
+// re-zeroes its counter.  (A lane-per-position layout -- one k row per lane,
+// then p.v by dims -- was measured slower at 1-2k positions: with 32 splits
+// a CTA has ~32 positions, which left one warp doing all of them.)
+constexpr int kAttnSplits = 32;
+
+template <int G, int kAttnWarps>
+__global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
+    const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
+    const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
+    int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
+    int form, __half* k_wr, __half* v_wr, int max_seq) {
+    // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
+    // vector: every CTA rotates its own query heads, and the current position's
+    // k (rotated) and v come from qkv in registers; the one CTA whose range
+    // holds that position also writes them to the caches (no CTA reads that row).
+    constexpr int HD = 128;
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (pos_out_of_range(*d_pos, max_seq)) return;
+    const int seq = *d_pos + 1;
+    const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
+    const int t0 = min(seq, split * chunk), t1 = min(seq, t0 + chunk);
+    const int kv_dim = NKV * HD;
+    const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
+
+    const bool fused = cos_tab != nullptr;
+    const int pos = seq - 1;
+    // RoPE of 4 dims held by this lane; dims d and d + HD/2 sit in lanes l and l ^ 16.
+    float rc[4], rs[4];
+    if (fused) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int d = (lane & 15) * 4 + e;
+            rc[e] = cos_tab[(size_t)pos * (HD / 2) + d];
+            rs[e] = sin_tab[(size_t)pos * (HD / 2) + d];
+        }
+    }
+    auto rotate = [&](float (&v)[4]) {   // v: this lane's 4 dims -> rotated, rounded to FP16
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            float o0, o1;
+            // (x, y) = (dim d, dim d + HD/2): lanes < 16 own x and keep o0, the others own y and keep o1
+            if (lane < 16) rope_pair(v[e], other, rc[e], rs[e], form, o0, o1);
+            else rope_pair(other, v[e], rc[e], rs[e], form, o0, o1);
+            v[e] = __half2float(__float2half_rn(lane < 16 ? o0 : o1));
+        }
+    };
+    auto load4 = [&](const __half* src, float (&v)[4]) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(src);
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        v[0] = __low2float(a);
+        v[1] = __high2float(a);
+        v[2] = __low2float(b);
+        v[3] = __high2float(b);
+    };
+    float qv[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        load4(q + (size_t)(kvh * G + g) * HD + lane * 4, qv[g]);
+        if (fused) rotate(qv[g]);
+    }
+    float kcur[4], vcur[4];
+    if (fused) {
+        const __half* kq = q + (size_t)NH * HD + (size_t)kvh * HD + lane * 4;
+        load4(kq, kcur);
+        rotate(kcur);
+        load4(kq + (size_t)NKV * HD, vcur);
+        if (warp == 0 && t0 <= pos && pos < t1) {
+            const size_t row = (size_t)pos * kv_dim + (size_t)kvh * HD + lane * 4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                k_wr[row + e] = __float2half_rn(kcur[e]);
+                v_wr[row + e] = __float2half_rn(vcur[e]);
+            }
+        }
+    }
+    float m[G], l[G], o[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+        o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+    }
+    auto load = [&](int t, float (&kf)[4], float (&vf)[4]) {
+        if (fused && t == pos) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                kf[e] = kcur[e];
+                vf[e] = vcur[e];
+            }
+            return;
+        }
+        const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
+        const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
+        const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
+        const __half2 k0 = *reinterpret_cast<const __half2*>(&kr.x), k1 = *reinterpret_cast<const __half2*>(&kr.y);
+        const __half2 v0 = *reinterpret_cast<const __half2*>(&vr.x), v1 = *reinterpret_cast<const __half2*>(&vr.y);
+        kf[0] = __low2float(k0);
+        kf[1] = __high2float(k0);
+        kf[2] = __low2float(k1);
+        kf[3] = __high2float(k1);
+        vf[0] = __low2float(v0);
+        vf[1] = __high2float(v0);
+        vf[2] = __low2float(v1);
+        vf[3] = __high2float(v1);
+    };
+    auto consume = [&](const float (&kf)[4], const float (&vf)[4]) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float sdot = qv[g][0] * kf[0];
+            sdot = fmaf(qv[g][1], kf[1], sdot);
+            sdot = fmaf(qv[g][2], kf[2], sdot);
+            sdot = fmaf(qv[g][3], kf[3], sdot);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+            const float sc = sdot * scale;
+            const float mn = fmaxf(m[g], sc);
+            const float corr = __expf(m[g] - mn);   // 0 on the first position (m = -inf)
+            const float pw = __expf(sc - mn);
+            l[g] = l[g] * corr + pw;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
+            m[g] = mn;
+        }
+    };
+    int t = t0 + warp;
+    for (; t + kAttnWarps < t1; t += 2 * kAttnWarps) {
+        float ka[4], va[4], kb[4], vb[4];
+        load(t, ka, va);
+        load(t + kAttnWarps, kb, vb);
+        consume(ka, va);
+        consume(kb, vb);
+    }
+    if (t < t1) {
+        float ka[4], va[4];
+        load(t, ka, va);
+        consume(ka, va);
+    }
+    // merge the 4 warps through shared memory, then this CTA's partial to the workspace
+    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
+    __shared__ float s_o[kAttnWarps][G][HD];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        if (lane == 0) {
+            s_m[warp][g] = m[g];
+            s_l[warp][g] = l[g];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s_o[warp][g][lane * 4 + e] = o[g][e];
+    }
+    __syncthreads();
+    constexpr int rec = 2 + HD;   // (m, l, o[HD]) per query head
+    float* my = part + ((size_t)kvh * kAttnSplits + split) * G * rec;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int g = i / HD, d = i % HD;
+        float mm = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
+        float ll = 0.f, oo = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
+            ll = fmaf(s_l[w][g], f, ll);
+            oo = fmaf(s_o[w][g][d], f, oo);
+        }
+        __stcg(my + g * rec + 2 + d, oo);
+        if (d == 0) {
+            __stcg(my + g * rec, mm);
+            __stcg(my + g * rec + 1, ll);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(counters + kvh, 1) == kAttnSplits - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* all = part + (size_t)kvh * kAttnSplits * G * rec;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int g = i / HD, d = i % HD;
+        float ms[kAttnSplits], ls[kAttnSplits], os[kAttnSplits];
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) {   // independent loads, all in flight
+            const float* r = all + (size_t)sp * G * rec + g * rec;
+            ms[sp] = ldcg_f32(r);
+            ls[sp] = ldcg_f32(r + 1);
+            os[sp] = ldcg_f32(r + 2 + d);
+        }
+        float mm = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ms[sp]);
+        float ll = 0.f, oo = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kAttnSplits; ++sp) {   // split order: deterministic
+            const float f = ms[sp] == -INFINITY ? 0.f : __expf(ms[sp] - mm);   // empty splits add nothing
+            ll = fmaf(ls[sp], f, ll);
+            oo = fmaf(os[sp], f, oo);
+        }
+        out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
+    }
+    if (threadIdx.x == 0) counters[kvh] = 0;   // leave the workspace counter at zero
+}
+
 
 // ------------------------------------------------------------- RMSNorm
 // The reference's rms_norm_kernel<half, 128> arithmetic (rmsnorm.cu:9-67):
@@ -330,7 +641,10 @@ extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const flo
 
 extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads, int max_seq) {
     if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_seq <= 0) return 0;
-    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_heads * max_seq * 4;
+    // the exact form's scores [NH][max_seq], or the fast form's split partials, whichever is larger
+    const size_t g = n_heads / n_kv_heads;
+    const size_t exact = (size_t)n_heads * max_seq * 4, fast = (size_t)n_kv_heads * kAttnSplits * g * (2 + 128) * 4;
+    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (exact > fast ? exact : fast);
 }
 
 static af_status attention_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
@@ -355,17 +669,75 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     // fused RoPE mode writes the current row of the caches (the caller's buffers are writable)
     __half* kw = cos_tab ? const_cast<__half*>(kh) : nullptr;
     __half* vw = cos_tab ? const_cast<__half*>(vh) : nullptr;
+    const size_t smem = attn_smem(n_heads / n_kv_heads, max_seq);
+    if (smem > kAttnSmemMax) return AF_ERR_UNSUPPORTED;   // the scores of the whole cache live in shared memory
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AF_ERR_CUDA;
+    static bool attr_set[kMaxDevices][kAttnMaxG + 1] = {};
     switch (n_heads / n_kv_heads) {
 #define AF_ATTN(GG)                                                                                       \
-    case GG:                                                                                              \
-        attention_kernel<GG><<<grid, GG * 128, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, scores, counters, \
-                                                        cos_tab, sin_tab, n_heads, max_seq, head_dim, kw, vw);      \
-        break;
+    case GG: {                                                                                            \
+        if (!attr_set[dev][GG]) {                                                                         \
+            cudaError_t ea = cudaFuncSetAttribute(attention_kernel<GG>,                                   \
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmemMax); \
+            if (ea != cudaSuccess) return cuda_fail(ea, "attention_kernel attributes");                   \
+            attr_set[dev][GG] = true;                                                                     \
+        }                                                                                                 \
+        attention_kernel<GG><<<grid, GG * 128, smem, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, scores, counters, \
+                                                           cos_tab, sin_tab, n_heads, max_seq, head_dim, kw, vw); \
+        break;                                                                                            \
+    }
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_kernel");
+}
+
+static af_status attention_split_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
+                                        void* out, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                                        void* workspace, size_t workspace_bytes, void* stream, const float* cos_tab,
+                                        const float* sin_tab) {
+    if (max_seq <= 0) return AF_ERR_INVALID;
+    if (q == nullptr || k_cache == nullptr || v_cache == nullptr || d_pos == nullptr || out == nullptr ||
+        n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+        return AF_ERR_INVALID;
+    if (head_dim != 128 || n_heads / n_kv_heads > kAttnMaxG) return AF_ERR_UNSUPPORTED;
+    if (!aligned(q, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) || !aligned(out, 2)) return AF_ERR_INVALID;
+    const size_t need = af_decode_attention_workspace_bytes(n_heads, n_kv_heads, max_seq);
+    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) return AF_ERR_WORKSPACE;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    int* counters = reinterpret_cast<int*>(ws + 256);
+    float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
+    constexpr int warps = 8;
+    const dim3 grid(kAttnSplits, n_kv_heads), block(warps * 32);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
+                 *vh = static_cast<const __half*>(v_cache);
+    __half* oh = static_cast<__half*>(out);
+    __half* kw = cos_tab ? const_cast<__half*>(kh) : nullptr;
+    __half* vw = cos_tab ? const_cast<__half*>(vh) : nullptr;
+    switch (n_heads / n_kv_heads) {
+#define AF_ATTN(GG) \
+    case GG:                                                                                                  \
+        attention_split_kernel<GG, warps><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part,      \
+                                                                  counters, cos_tab, sin_tab, n_heads, kRopeForm, \
+                                                                  kw, vw, max_seq);                            \
+        break;
+        AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
+#undef AF_ATTN
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_split_kernel");
+}
+
+extern "C" af_status af_decode_rope_attention_fast(void* qkv, const float* cos_tab, const float* sin_tab,
+                                                  const int* d_pos, void* k_cache, void* v_cache, void* out,
+                                                  int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                                                  void* workspace, size_t workspace_bytes, void* stream) {
+    if (cos_tab == nullptr || sin_tab == nullptr) return AF_ERR_INVALID;
+    return attention_split_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, max_seq,
+                                  workspace, workspace_bytes, stream, cos_tab, sin_tab);
 }
 
 extern "C" af_status af_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,

@@ -590,7 +590,10 @@ def run_decode(args, device, local):
         R.afref_engine_destroy(h)
         return 0
     from atomflow_b200.decode import DecodeEngine
-    eng = DecodeEngine(path)
+    eng = DecodeEngine(path, mode=args.decode_mode)
+    config["engine"] = (f"C++ af_engine, {args.decode_mode} mode: " +
+                        ("every kernel bit-identical to the reference's" if args.decode_mode == "exact" else
+                         "fused tensor-core projections, split-KV attention"))
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, 65536, DECODE_POS).tolist()
     g = eng.capture(advance=True)
@@ -621,24 +624,27 @@ def run_decode(args, device, local):
     t1 = time.time()
     ms = ev0.elapsed_time(ev1) / args.steps
     clocks = sampler.summary(t0, t1)
-    # end to end: each step the host sends the token and reads the next one (pinned, inside the graph)
+    # end to end: each step the host sends the token from pinned memory, the
+    # captured step runs, and the next token returns to pinned memory
+    cudart = ctypes.CDLL("libcudart.so.12")
+    cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
     tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
     tok_back = torch.zeros(1, dtype=torch.int32).pin_memory()
-    ge = torch.cuda.CUDAGraph()
-    eng.current_pos = DECODE_POS
-    eng.stream.synchronize()
-    with torch.cuda.graph(ge, stream=eng.stream):
-        eng.d_token.copy_(tok_h, non_blocking=True)
-        eng._launch_step(eng.stream.cuda_stream, advance=True)
-        tok_back.copy_(eng.d_token, non_blocking=True)
+    est = eng.stream.cuda_stream
+
+    def e2e_step():
+        cudart.cudaMemcpyAsync(eng.d_token, tok_h.data_ptr(), 4, 1, est)
+        eng.replay(g)
+        cudart.cudaMemcpyAsync(tok_back.data_ptr(), eng.d_token, 4, 2, est)
+
     eng.current_pos = DECODE_POS
     for _ in range(3):
-        eng.replay(ge)
+        e2e_step()
     eng.current_pos = DECODE_POS
     eng.stream.synchronize()
     ev0.record(eng.stream)
     for _ in range(args.steps):
-        eng.replay(ge)
+        e2e_step()
     ev1.record(eng.stream)
     eng.stream.synchronize()
     e2e_ms = ev0.elapsed_time(ev1) / args.steps
@@ -679,8 +685,8 @@ def run_decode(args, device, local):
                 "gpu_launches": eng.launches_per_step * args.steps, "tokens": tokens,
                 "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 5),
                         "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                        "path": "DecodeEngine over the C ABI: token H2D from pinned memory, the step, next token D2H "
-                                "to pinned memory, one CUDA graph per step"}})
+                        "path": "af_engine (C++) over the C ABI: token H2D from pinned memory, the captured step, next "
+                                "token D2H to pinned memory, every step"}})
     print(json.dumps(out))
     return 0
 
@@ -698,6 +704,8 @@ def main():
                     help="chain: tensor-core dot products (fast) or the reference kernel's FP32 FMA order (exact)")
     ap.add_argument("--launch", choices=["chain", "per-gemv"], default="per-gemv",
                     help="one-token GEMVs on one GPU: one persistent launch per step (chain) or one launch per GEMV")
+    ap.add_argument("--decode-mode", choices=["exact", "fast"], default="fast",
+                    help="decode: kernels bit-identical to the reference's (exact) or the fused fast forms")
     ap.add_argument("--no-token-check", action="store_true",
                     help="decode: skip comparing 64 greedy tokens with the reference engine")
     ap.add_argument("--layers", type=int, default=NLAYERS,

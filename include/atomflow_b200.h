@@ -226,6 +226,13 @@ af_status af_decode_attention(const void* q, const void* k_cache, const void* v_
 af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                    void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
                                    int head_dim, int max_seq, void* workspace, size_t workspace_bytes, void* stream);
+/* The same step as af_decode_rope_attention (and the same workspace) with a
+ * split-KV online softmax: every output within 2 FP16 ulp / 2e-3 relative of
+ * FP64, not the reference's summation order.  A fast form for throughput. */
+af_status af_decode_rope_attention_fast(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
+                                        void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
+                                        int head_dim, int max_seq, void* workspace, size_t workspace_bytes,
+                                        void* stream);
 af_status af_rmsnorm(const void* x, const float* norm_w, float eps, void* out, int K, void* stream);
 af_status af_decode_advance(int* d_pos, int by, void* stream);
 
@@ -287,6 +294,51 @@ af_status af_gemv_chain(const af_chain_op* ops, int n_ops, void* workspace, size
  * its summation order, so not bit-identical to it.  Same arguments. */
 af_status af_gemv_chain_fast(const af_chain_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
                              void* stream);
+
+/* -------------------------------------------------------- decode engine ---
+ * A whole greedy decode step of a model in the reference's .bin format
+ * (tools/quantize_weights.py:320-427; read as include/memory/weight_loader.h
+ * and src/core/engine.cu:103-147 read it), driven from C++ with no Python:
+ * the interface of the reference's AtomFlowEngine (include/core/engine.h:
+ * initialize / inject_token / forward_pass / get_output_token / current_pos_),
+ * with the token id and the position kept in device ints so that a captured
+ * step replays token after token.  The engine is the one part of this library
+ * that allocates device memory: at create, its weight arena (the file, copied
+ * once), KV cache, activations and workspaces -- as the reference engine's
+ * initialize does (engine.cu:56-234); nothing allocates afterwards.
+ *   AF_ENGINE_EXACT  every kernel bit-identical to the reference's: projection
+ *                    chains (af_gemv_chain), attention, norms, SwiGLU,
+ *                    residual, RoPE, embedding; lm_head + argmax as
+ *                    af_lm_head_gemv (the reference's is a cuBLAS call)
+ *   AF_ENGINE_FAST   the fused tensor-core projections and the split-KV
+ *                    attention (af_decode_rope_attention_fast)
+ * argmax_mode: AF_ARGMAX_REF_COMPAT (the reference's ids < 65536) or TRUE.
+ * One engine per host thread at a time; calls are ordered on its stream. */
+typedef struct af_engine af_engine;
+typedef enum af_engine_mode { AF_ENGINE_EXACT = 0, AF_ENGINE_FAST = 1 } af_engine_mode;
+af_status af_engine_create(const char* bin_path, int max_seq, af_engine_mode mode, af_argmax_mode argmax_mode,
+                           af_engine** out);
+af_status af_engine_destroy(af_engine* e);
+/* dims[9]: dim, ffn, layers, heads, kv heads, vocab, max_seq, launches per step (without the
+ * position advance), file size in MiB. */
+af_status af_engine_info(const af_engine* e, int* dims);
+af_status af_engine_set_position(af_engine* e, int pos);
+af_status af_engine_get_position(af_engine* e, int* pos);
+af_status af_engine_inject_token(af_engine* e, int token);
+af_status af_engine_output_token(af_engine* e, int* token);
+/* One step launched eagerly (advance != 0: then *d_pos += 1 on the device). */
+af_status af_engine_step(af_engine* e, int advance);
+/* Captures one step (advance != 0: with the position increment) as a CUDA graph
+ * owned by the engine (replacing any earlier one); the first eager step must
+ * have run.  af_engine_replay launches it n times on the engine's stream. */
+af_status af_engine_capture(af_engine* e, int advance);
+af_status af_engine_replay(af_engine* e, int n);
+af_status af_engine_synchronize(af_engine* e);
+/* The engine's stream (cudaStream_t), device token / position ints, FP32 logits [vocab]. */
+void* af_engine_stream(af_engine* e);
+int* af_engine_device_token(af_engine* e);
+int* af_engine_device_position(af_engine* e);
+const float* af_engine_logits(af_engine* e);
 
 /* ----------------------------------------------- argmax, no allocation ---
  * No counterpart in the reference.  The same argmax as af_argmax_f32 for

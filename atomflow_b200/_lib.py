@@ -104,6 +104,7 @@ C_SYMBOLS = {
     "af_gemv_chain": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
     "af_gemv_chain_fast": (_i, [ctypes.c_void_p, _i, _vp, _sz, _vp]),
     "af_engine_create": (_i, [ctypes.c_char_p, _i, _i, _i, ctypes.POINTER(ctypes.c_void_p)]),
+    "af_engine_create_tp": (_i, [ctypes.c_char_p, _i, _i, _vp, ctypes.POINTER(ctypes.c_void_p)]),
     "af_engine_destroy": (_i, [_vp]),
     "af_engine_info": (_i, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "af_engine_set_position": (_i, [_vp, _i]),

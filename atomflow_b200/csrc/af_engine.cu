@@ -94,9 +94,100 @@ struct af_engine {
     cudaGraphExec_t graph = nullptr;
     bool stepped = false;
     int launches = 0;
+    // tensor parallelism (world > 1): this rank's heads, FFN rows and vocabulary rows
+    af_tp_comm* comm = nullptr;
+    int rank = 0, world = 1;
+    int NHl = 0, NKVl = 0, FFNl = 0, v0 = 0, v1 = 0;
+    std::vector<void*> owned;   // per-tensor device buffers of a sharded load
 };
 
 namespace {
+
+// Tensor parallelism: copies this rank's part of every tensor out of the mapped
+// file into its own device buffer (Megatron split; the row-split K shards hold
+// whole 128-wide scale groups, so their scales are the full matrix's):
+//   qkv   rows of the rank's query heads, then of its kv heads' k and v
+//   o     the columns of the rank's heads (K split)
+//   gate, up   rows [r F/w, (r+1) F/w)
+//   down  columns [r F/w, (r+1) F/w) (K split)
+//   lm_head    vocabulary rows [r V/w, (r+1) V/w)
+// The embedding and the norms are replicated.
+af_status load_shards(af_engine* e, const unsigned char* f, size_t embed_off, size_t fnorm_off, size_t lm_off,
+                      const std::vector<size_t>& blocks) {
+    const Header& h = e->h;
+    const int w = e->world, r = e->rank, HD = e->HD;
+    cudaError_t ce = cudaSuccess;
+    // rows x width bytes, source pitch spitch, from file offset src
+    auto copy2d = [&](size_t src, size_t width, size_t rows, size_t spitch) -> unsigned char* {
+        unsigned char* d = nullptr;
+        if (ce != cudaSuccess) return nullptr;
+        ce = cudaMalloc(&d, std::max<size_t>(width * rows, 16));
+        if (ce != cudaSuccess) return nullptr;
+        e->owned.push_back(d);
+        ce = cudaMemcpy2D(d, width, f + src, spitch, width, rows, cudaMemcpyHostToDevice);
+        return d;
+    };
+    const size_t D = h.dim, F = h.ffn, G = D / kGroup, GF = F / kGroup;
+    e->embed = reinterpret_cast<const float*>(copy2d(embed_off, (size_t)h.vocab * D * 4, 1, 0));
+    e->final_norm = reinterpret_cast<const float*>(copy2d(fnorm_off, D * 4, 1, 0));
+    e->lm_head = reinterpret_cast<const uint16_t*>(
+        copy2d(lm_off + (size_t)e->v0 * D * 2, (size_t)(e->v1 - e->v0) * D * 2, 1, 0));
+    e->layers.resize(h.n_layers);
+    const int hq = e->NHl, hk = e->NKVl;
+    for (int l = 0; l < h.n_layers && ce == cudaSuccess; ++l) {
+        const size_t* b = &blocks[(size_t)l * 12];
+        Layer& L = e->layers[l];
+        L.in_norm = reinterpret_cast<const float*>(copy2d(b[0], D * 4, 1, 0));
+        L.post_norm = reinterpret_cast<const float*>(copy2d(b[1], D * 4, 1, 0));
+        // qkv: three row ranges packed [Q_r | K_r | V_r]
+        {
+            const size_t rq = (size_t)hq * HD, rk = (size_t)hk * HD;
+            const size_t starts[3] = {(size_t)r * rq, (size_t)h.n_heads * HD + (size_t)r * rk,
+                                      (size_t)(h.n_heads + h.n_kv_heads) * HD + (size_t)r * rk};
+            const size_t counts[3] = {rq, rk, rk};
+            unsigned char* wq = nullptr;
+            unsigned char* sq = nullptr;
+            const size_t rows = rq + 2 * rk;
+            if (ce == cudaSuccess) ce = cudaMalloc(&wq, rows * D);
+            if (ce == cudaSuccess) { e->owned.push_back(wq); ce = cudaMalloc(&sq, rows * G * 2); }
+            if (ce == cudaSuccess) e->owned.push_back(sq);
+            size_t at_row = 0;
+            for (int p = 0; p < 3 && ce == cudaSuccess; ++p) {
+                ce = cudaMemcpy(wq + at_row * D, f + b[2] + starts[p] * D, counts[p] * D, cudaMemcpyHostToDevice);
+                if (ce == cudaSuccess)
+                    ce = cudaMemcpy(sq + at_row * G * 2, f + b[3] + starts[p] * G * 2, counts[p] * G * 2,
+                                    cudaMemcpyHostToDevice);
+                at_row += counts[p];
+            }
+            L.qkv = {wq, reinterpret_cast<const uint16_t*>(sq), (int)rows, (int)D};
+        }
+        // o: K split by heads
+        {
+            const size_t kc = D / w;
+            unsigned char* wo = copy2d(b[4] + (size_t)r * kc, kc, D, D);
+            unsigned char* so = copy2d(b[5] + (size_t)r * (G / w) * 2, (G / w) * 2, D, G * 2);
+            L.o = {wo, reinterpret_cast<const uint16_t*>(so), (int)D, (int)kc};
+        }
+        // gate, up: rows
+        {
+            const size_t rows = F / w;
+            unsigned char* wg = copy2d(b[6] + (size_t)r * rows * D, rows * D, 1, 0);
+            unsigned char* sg = copy2d(b[7] + (size_t)r * rows * G * 2, rows * G * 2, 1, 0);
+            unsigned char* wu = copy2d(b[8] + (size_t)r * rows * D, rows * D, 1, 0);
+            unsigned char* su = copy2d(b[9] + (size_t)r * rows * G * 2, rows * G * 2, 1, 0);
+            L.gate = {wg, reinterpret_cast<const uint16_t*>(sg), (int)rows, (int)D};
+            L.up = {wu, reinterpret_cast<const uint16_t*>(su), (int)rows, (int)D};
+        }
+        // down: K split
+        {
+            const size_t kc = F / w;
+            unsigned char* wd = copy2d(b[10] + (size_t)r * kc, kc, D, F);
+            unsigned char* sd = copy2d(b[11] + (size_t)r * (GF / w) * 2, (GF / w) * 2, D, GF * 2);
+            L.down = {wd, reinterpret_cast<const uint16_t*>(sd), (int)D, (int)kc};
+        }
+    }
+    return ce == cudaSuccess ? AF_OK : af::cuda_fail(ce, "af_engine_create_tp: weights");
+}
 
 // Reads the file into the device arena and points every tensor into it.
 // Block order (weight_loader.h next_block, engine.cu:103-147): embedding FP32
@@ -153,6 +244,24 @@ af_status load_file(af_engine* e, const char* path) {
     plan.lm_head = take(V * D * 2);
     (void)F;
     if (st == AF_OK && size < off) st = AF_ERR_INVALID;
+    // this rank's part of the model (the whole model when world == 1)
+    const int w = e->world;
+    if (st == AF_OK && (h.n_heads % w || h.n_kv_heads % w || h.ffn % (kGroup * w) || h.dim % (kGroup * w)))
+        st = AF_ERR_UNSUPPORTED;   // heads, FFN rows and K shards must split evenly into whole scale groups
+    e->NHl = h.n_heads / w;
+    e->NKVl = h.n_kv_heads / w;
+    e->FFNl = h.ffn / w;
+    e->v0 = (int)((long long)e->rank * h.vocab / w);
+    e->v1 = (int)((long long)(e->rank + 1) * h.vocab / w);
+    e->QD = e->NHl * e->HD;
+    e->KVD = e->NKVl * e->HD;
+    e->QKV = e->QD + 2 * e->KVD;
+    if (st == AF_OK && e->world > 1) {
+        e->file_bytes = off;
+        st = load_shards(e, f, plan.embed, plan.final_norm, plan.lm_head, plan.blocks);
+        munmap(map, size);
+        return st;
+    }
     if (st == AF_OK) {
         e->file_bytes = off;
         cudaError_t ce = cudaMalloc(&e->arena, off - kAlign);
@@ -206,7 +315,7 @@ af_status launch_step(af_engine* e, bool advance) {
             if (r == AF_OK && l < h.n_layers) {
                 Layer& L = e->layers[l];
                 r = af_decode_rope_attention(e->qkv, e->cos_tab, e->sin_tab, e->d_pos, L.k_cache, L.v_cache, e->attn,
-                                             h.n_heads, h.n_kv_heads, e->HD, e->max_seq, e->attn_ws, e->attn_ws_bytes,
+                                             e->NHl, e->NKVl, e->HD, e->max_seq, e->attn_ws, e->attn_ws_bytes,
                                              st);
                 ++n;
             }
@@ -218,24 +327,30 @@ af_status launch_step(af_engine* e, bool advance) {
                                       AF_SCALE_GROUP_F16, nullptr, st);
             if (r == AF_OK)
                 r = af_decode_rope_attention_fast(e->qkv, e->cos_tab, e->sin_tab, e->d_pos, L.k_cache, L.v_cache,
-                                                  e->attn, h.n_heads, h.n_kv_heads, e->HD, e->max_seq, e->attn_ws,
+                                                  e->attn, e->NHl, e->NKVl, e->HD, e->max_seq, e->attn_ws,
                                                   e->attn_ws_bytes, st);
             if (r == AF_OK)
-                r = af_w8a16_gemv_residual(e->attn, L.o.w, L.o.s, e->x, L.o.N, L.o.K, kGroup, AF_SCALE_GROUP_F16,
-                                           nullptr, st);
+                r = e->comm ? af_w8a16_gemv_allreduce_residual(e->attn, L.o.w, L.o.s, e->x, L.o.N, L.o.K, kGroup,
+                                                               AF_SCALE_GROUP_F16, e->comm, st)
+                            : af_w8a16_gemv_residual(e->attn, L.o.w, L.o.s, e->x, L.o.N, L.o.K, kGroup,
+                                                     AF_SCALE_GROUP_F16, nullptr, st);
             if (r == AF_OK)
                 r = af_rmsnorm_w8a16_swiglu(e->x, L.post_norm, kNormEps, L.gate.w, L.gate.s, L.up.w, L.up.s, e->hbuf,
                                             L.gate.N, L.gate.K, kGroup, AF_SCALE_GROUP_F16, nullptr, nullptr, st);
             if (r == AF_OK)
-                r = af_w8a16_gemv_residual(e->hbuf, L.down.w, L.down.s, e->x, L.down.N, L.down.K, kGroup,
-                                           AF_SCALE_GROUP_F16, nullptr, st);
+                r = e->comm ? af_w8a16_gemv_allreduce_residual(e->hbuf, L.down.w, L.down.s, e->x, L.down.N,
+                                                               L.down.K, kGroup, AF_SCALE_GROUP_F16, e->comm, st)
+                            : af_w8a16_gemv_residual(e->hbuf, L.down.w, L.down.s, e->x, L.down.N, L.down.K, kGroup,
+                                                     AF_SCALE_GROUP_F16, nullptr, st);
             n += 5;
         }
     }
     if (r == AF_OK) r = af_rmsnorm(e->x, e->final_norm, kNormEps, e->xn, h.dim, st);
     if (r == AF_OK)
-        r = af_lm_head_gemv(e->xn, e->lm_head, AF_W_F16, nullptr, e->logits, h.vocab, h.dim, e->d_token, e->amode,
-                            e->lm_ws, e->lm_ws_bytes, st);
+        r = e->comm ? af_lm_head_gemv_tp(e->xn, e->lm_head, AF_W_F16, nullptr, e->logits, e->v1 - e->v0, h.dim, e->v0,
+                                         e->d_token, e->amode, e->lm_ws, e->lm_ws_bytes, e->comm, st)
+                    : af_lm_head_gemv(e->xn, e->lm_head, AF_W_F16, nullptr, e->logits, h.vocab, h.dim, e->d_token,
+                                      e->amode, e->lm_ws, e->lm_ws_bytes, st);
     n += 2;
     if (r == AF_OK && advance) r = af_decode_advance(e->d_pos, 1, st);
     e->launches = n;
@@ -310,6 +425,7 @@ extern "C" af_status af_engine_destroy(af_engine* e) {
     if (e == nullptr) return AF_ERR_INVALID;
     if (e->graph) cudaGraphExecDestroy(e->graph);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void* p : e->owned) cudaFree(p);
     cudaFree(e->arena);
     cudaFree(e->acts);
     cudaFree(e->kv);
@@ -318,13 +434,23 @@ extern "C" af_status af_engine_destroy(af_engine* e) {
     return AF_OK;
 }
 
-extern "C" af_status af_engine_create(const char* bin_path, int max_seq, af_engine_mode mode, af_argmax_mode argmax_mode,
-                                      af_engine** out) {
+static af_status engine_create(const char* bin_path, int max_seq, af_engine_mode mode, af_argmax_mode argmax_mode,
+                               af_tp_comm* comm, af_engine** out) {
     if (bin_path == nullptr || out == nullptr || max_seq <= 0) return AF_ERR_INVALID;
     if (mode != AF_ENGINE_EXACT && mode != AF_ENGINE_FAST) return AF_ERR_INVALID;
     if (argmax_mode != AF_ARGMAX_TRUE && argmax_mode != AF_ARGMAX_REF_COMPAT) return AF_ERR_INVALID;
     *out = nullptr;
     af_engine* e = new af_engine();
+    if (comm != nullptr) {
+        int dev = -1;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) {
+            delete e;
+            return AF_ERR_INVALID;   // the engine runs on the communicator's device
+        }
+        e->comm = comm->world > 1 ? comm : nullptr;
+        e->rank = comm->rank;
+        e->world = comm->world;
+    }
     e->max_seq = max_seq;
     e->mode = mode;
     e->amode = argmax_mode;
@@ -337,12 +463,12 @@ extern "C" af_status af_engine_create(const char* bin_path, int max_seq, af_engi
     }
     if (st == AF_OK) {
         // activations, state and workspaces: one arena, 256-byte aligned pieces
-        e->attn_ws_bytes = af_decode_attention_workspace_bytes(h.n_heads, h.n_kv_heads, max_seq);
-        e->lm_ws_bytes = af_lm_head_workspace_bytes(h.vocab, h.dim, AF_W_F16);
+        e->attn_ws_bytes = af_decode_attention_workspace_bytes(e->NHl, e->NKVl, max_seq);
+        e->lm_ws_bytes = af_lm_head_workspace_bytes(e->v1 - e->v0, h.dim, AF_W_F16);
         e->chain_ws_bytes = af_chain_workspace_bytes(4);
         const size_t half_tab = (size_t)max_seq * (e->HD / 2) * 4;
         const size_t sizes[] = {(size_t)h.dim * 2, (size_t)h.dim * 2, (size_t)e->QKV * 2, (size_t)e->QD * 2,
-                                (size_t)h.ffn * 2, (size_t)h.vocab * 4, 4, 4, half_tab, half_tab,
+                                (size_t)e->FFNl * 2, (size_t)(e->v1 - e->v0) * 4, 4, 4, half_tab, half_tab,
                                 e->attn_ws_bytes, e->lm_ws_bytes, e->chain_ws_bytes};
         size_t total = 0;
         for (size_t b : sizes) total += pad(b);
@@ -392,12 +518,26 @@ extern "C" af_status af_engine_create(const char* bin_path, int max_seq, af_engi
             build_segments(e);
         }
     }
+    if (st == AF_OK && e->comm != nullptr && e->comm->nmax < h.dim) st = AF_ERR_INVALID;   // all-reduce rows
     if (st != AF_OK) {
         af_engine_destroy(e);
         return st;
     }
     *out = e;
     return AF_OK;
+}
+
+extern "C" af_status af_engine_create(const char* bin_path, int max_seq, af_engine_mode mode, af_argmax_mode argmax_mode,
+                                      af_engine** out) {
+    return engine_create(bin_path, max_seq, mode, argmax_mode, nullptr, out);
+}
+
+extern "C" af_status af_engine_create_tp(const char* bin_path, int max_seq, af_argmax_mode argmax_mode,
+                                         af_tp_comm* comm, af_engine** out) {
+    if (comm == nullptr) return AF_ERR_INVALID;
+    for (int r = 0; r < comm->world; ++r)
+        if (comm->peer[r] == nullptr) return AF_ERR_INVALID;   // peers not opened
+    return engine_create(bin_path, max_seq, AF_ENGINE_FAST, argmax_mode, comm, out);
 }
 
 extern "C" af_status af_engine_info(const af_engine* e, int* dims) {

@@ -26,7 +26,10 @@ MODES = {"exact": 0, "fast": 1}
 
 
 class DecodeEngine:
-    def __init__(self, path, device="cuda", max_seq_len=MAX_SEQ_LEN, true_argmax=False, mode="exact"):
+    def __init__(self, path, device="cuda", max_seq_len=MAX_SEQ_LEN, true_argmax=False, mode="exact", comm=None):
+        """comm: an atomflow_b200.tp.TpComm -- this process's rank of a
+        tensor-parallel engine (fast mode; every rank ends each step with the
+        same token)."""
         import torch
         self.L = lib()
         if mode not in MODES:
@@ -43,8 +46,16 @@ class DecodeEngine:
         self.max_seq = max_seq_len
         self.mode = mode
         h = ctypes.c_void_p()
-        check(self.L.af_engine_create(str(path).encode(), max_seq_len, MODES[mode], 0 if true_argmax else 1,
-                                      ctypes.byref(h)), "af_engine_create")
+        amode = 0 if true_argmax else 1
+        if comm is not None and comm.world > 1:
+            if mode != "fast":
+                raise ValueError("a tensor-parallel engine runs the fast mode")
+            check(self.L.af_engine_create_tp(str(path).encode(), max_seq_len, amode, comm.h, ctypes.byref(h)),
+                  "af_engine_create_tp")
+        else:
+            check(self.L.af_engine_create(str(path).encode(), max_seq_len, MODES[mode], amode, ctypes.byref(h)),
+                  "af_engine_create")
+        self.comm = comm
         self.h = h
         self.stream = torch.cuda.ExternalStream(self.L.af_engine_stream(h), device=torch.cuda.current_device())
         self.launches_per_step = None

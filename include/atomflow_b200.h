@@ -319,6 +319,16 @@ typedef enum af_engine_mode { AF_ENGINE_EXACT = 0, AF_ENGINE_FAST = 1 } af_engin
 af_status af_engine_create(const char* bin_path, int max_seq, af_engine_mode mode, af_argmax_mode argmax_mode,
                            af_engine** out);
 af_status af_engine_destroy(af_engine* e);
+/* Tensor-parallel engine: rank comm->rank of comm->world (af_tp_create /
+ * af_tp_open_peers, max_n >= dim), one process per GPU with that GPU current.
+ * Megatron split: QKV by heads, gate/up by rows, O and down along K with the
+ * partial outputs summed over the ranks inside the projection kernel over
+ * NVLink peer memory (af_w8a16_gemv_allreduce_residual), the lm_head by
+ * vocabulary rows with the argmax exchanged in its kernel (af_lm_head_gemv_tp):
+ * every rank ends the step with the same token.  Fast mode only (a sum split
+ * over ranks cannot keep the reference's summation order). */
+af_status af_engine_create_tp(const char* bin_path, int max_seq, af_argmax_mode argmax_mode, af_tp_comm* comm,
+                              af_engine** out);
 /* dims[9]: dim, ffn, layers, heads, kv heads, vocab, max_seq, launches per step (without the
  * position advance), file size in MiB. */
 af_status af_engine_info(const af_engine* e, int* dims);

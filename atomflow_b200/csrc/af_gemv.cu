@@ -614,9 +614,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                          smem_u32(&s_xbar));
         }
     }
-    __shared__ unsigned s_ep;   // this launch's epoch (tensor-parallel epilogue)
-    if (p.tp_world > 1 && threadIdx.x == 0)
-        s_ep = ldcg_s32(reinterpret_cast<const int*>(p.tp_buf[p.tp_rank] + TpLayout::epoch) + cta) + 1;
+    // tensor-parallel epilogue: row r's tag this launch is its epoch + 1
+    const unsigned* row_ep = p.tp_world > 1
+        ? reinterpret_cast<const unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::row_epoch(p.tp_nmax)) : nullptr;
     cp_async_wait<0>();    // staged scales (and the early ring slots) have landed
     __syncthreads();       // everyone's staged scales are visible
     if (!mbar_wait_bounded(smem_u32(&s_xbar), 0, 2000000000ull))
@@ -746,16 +746,18 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
             b *= r1 < row1 ? __ldg(rs + r1) : 0.f;
         }
         if (p.tp_world > 1 && !p.tp_arg) {
-            // this rank's partial of rows r0, r1, tagged with the epoch, into
-            // every rank's buffer (NVLink stores to the peers)
-            const size_t slot = ((size_t)(s_ep & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
-            const unsigned long long ta = ((unsigned long long)s_ep << 32) | __float_as_uint(a);
-            const unsigned long long tb = ((unsigned long long)s_ep << 32) | __float_as_uint(b);
+            // this rank's partial of rows r0, r1, tagged with each row's
+            // epoch, into every rank's buffer (NVLink stores to the peers)
+            const unsigned ea = r0 < row1 ? __ldcg(row_ep + r0) + 1u : 0u;
+            const unsigned eb = r1 < row1 ? __ldcg(row_ep + r1) + 1u : 0u;
+            const size_t sa = ((size_t)(ea & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
+            const size_t sb = ((size_t)(eb & 1) * kTpMaxRanks + p.tp_rank) * p.tp_nmax;
+            const unsigned long long ta = ((unsigned long long)ea << 32) | __float_as_uint(a);
+            const unsigned long long tb = ((unsigned long long)eb << 32) | __float_as_uint(b);
             for (int rr = 0; rr < p.tp_world; ++rr) {
-                unsigned long long* part =
-                    reinterpret_cast<unsigned long long*>(p.tp_buf[rr] + TpLayout::part) + slot;
-                if (r0 < row1) st_relaxed_sys_u64(part + r0, ta);
-                if (r1 < row1) st_relaxed_sys_u64(part + r1, tb);
+                unsigned long long* part = reinterpret_cast<unsigned long long*>(p.tp_buf[rr] + TpLayout::part);
+                if (r0 < row1) st_relaxed_sys_u64(part + sa + r0, ta);
+                if (r1 < row1) st_relaxed_sys_u64(part + sb + r1, tb);
             }
         } else if (p.y != nullptr) {
             if (p.y_f32) {
@@ -917,18 +919,21 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
 
     if (p.tp_world > 1 && !p.tp_arg) {
         // Sum this CTA's rows over the ranks, in rank order: each word is
-        // polled (bounded) until it carries this launch's epoch.  A peer is at
-        // most one launch ahead (it cannot finish a launch without our
-        // partials of it), so the other parity half is never overwritten early.
-        const unsigned ep = s_ep;
-        const unsigned long long* part =
-            reinterpret_cast<const unsigned long long*>(p.tp_buf[p.tp_rank] + TpLayout::part) +
-            (size_t)(ep & 1) * kTpMaxRanks * p.tp_nmax;
+        // polled (bounded) until it carries the row's epoch.  A peer is at
+        // most one launch ahead on any row (it cannot finish a launch without
+        // our partials of it), so the other parity half is never overwritten
+        // early.  The barrier orders every emitting thread's epoch read before
+        // the thread that owns the row here bumps it.
+        __syncthreads();
+        unsigned* my_ep = reinterpret_cast<unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::row_epoch(p.tp_nmax));
+        const unsigned long long* part = reinterpret_cast<const unsigned long long*>(p.tp_buf[p.tp_rank] + TpLayout::part);
         bool late = false;
         for (int r = row0 + threadIdx.x; r < row1; r += kThreads) {
+            const unsigned ep = __ldcg(my_ep + r) + 1u;
+            const unsigned long long* half_r = part + (size_t)(ep & 1) * kTpMaxRanks * p.tp_nmax + r;
             float acc_r = 0.f;
             for (int rr = 0; rr < p.tp_world; ++rr) {
-                const unsigned long long* wp = part + (size_t)rr * p.tp_nmax + r;
+                const unsigned long long* wp = half_r + (size_t)rr * p.tp_nmax;
                 unsigned long long v = ld_relaxed_sys_u64(wp);
                 if ((unsigned)(v >> 32) != ep && !late) {
                     const uint64_t t0 = globaltimer_ns();
@@ -939,15 +944,13 @@ __global__ void __launch_bounds__(kWarps * 32, kMinCtas) gemv_fp8_m1_kernel(cons
                 }
                 acc_r += __uint_as_float((unsigned)v);
             }
+            __stcg(my_ep + r, ep);
             __half yh = __float2half_rn(acc_r);
             if (p.aux != nullptr) p.aux[r] = yh;
             if (p.res != nullptr) yh = __float2half_rn(__half2float(p.res[r]) + __half2float(yh));
             static_cast<__half*>(p.y)[r] = yh;
         }
         if (late) atomicOr(reinterpret_cast<int*>(p.tp_buf[p.tp_rank] + TpLayout::status), 1);
-        __syncthreads();
-        if (threadIdx.x == 0)
-            reinterpret_cast<unsigned*>(p.tp_buf[p.tp_rank] + TpLayout::epoch)[cta] = ep;
     }
 
     if (p.arg_out != nullptr) {
@@ -1255,7 +1258,7 @@ af_status run_gemv(int wk, const __half* x, const uint8_t* w, const void* s, voi
         prm.tp_arg = arg_out != nullptr;
         prm.arg_off = tp_arg_off;
         for (int r = 0; r < tp->world; ++r) prm.tp_buf[r] = tp->peer[r];
-        if (arg_out == nullptr && (pl.grid > kTpMaxCtas || N > tp->nmax)) return AF_ERR_UNSUPPORTED;
+        if (arg_out == nullptr && N > tp->nmax) return AF_ERR_UNSUPPORTED;
     }
     // Shared memory: the ring, staged x and scales (when they fit), warp partials.
     const size_t ring = (size_t)kWarpsPerCta * kRingSlots * 1024;

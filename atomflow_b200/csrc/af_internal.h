@@ -70,20 +70,24 @@ constexpr int kTpMaxCtas = 256;
 // size, and each rank maps all of them (CUDA IPC or same-process pointers):
 //   [0, 256)            status word (bit 0: a bounded wait gave up) at 0; lm_head
 //                       argmax exchange epoch at 4
-//   [256, +1 KB)        per-CTA launch epoch of this rank
+//   [256, +1 KB)        unused
 //   [1280, +256)        lm_head argmax pairs [epoch parity][source rank] as two
 //                       64-bit words {epoch, FP32 max} {epoch, global index}
 //   [.., +2*8*nmax*8)   partials [epoch parity][source rank][nmax], each a 64-bit
 //                       word {launch epoch : 32, FP32 bits : 32}: the data carries
 //                       its own flag, so a reader polls the word itself and no
 //                       fence or separate flag store is needed
+//   [.., +nmax*4)       per-row epoch of this rank: how many all-reduces row r
+//                       has taken part in.  Keyed by row, not by CTA, so the tag
+//                       of a row alternates parity on every launch that touches
+//                       it whatever grid each launch uses
 struct TpLayout {
     static constexpr size_t status = 0;
     static constexpr size_t lm_epoch = 4;
-    static constexpr size_t epoch = 256;
     static constexpr size_t lm_pair = 256 + kTpMaxCtas * 4;
     static constexpr size_t part = lm_pair + 2 * kTpMaxRanks * 16;
-    static size_t bytes(int nmax) { return part + (size_t)2 * kTpMaxRanks * nmax * 8; }
+    __host__ __device__ static size_t row_epoch(int nmax) { return part + (size_t)2 * kTpMaxRanks * nmax * 8; }
+    __host__ __device__ static size_t bytes(int nmax) { return row_epoch(nmax) + (((size_t)nmax * 4 + 15) & ~(size_t)15); }
 };
 }  // namespace af
 

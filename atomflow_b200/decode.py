@@ -35,7 +35,8 @@ class DecodeEngine:
         if mode not in MODES:
             raise ValueError(f"mode must be one of {list(MODES)}")
         dev = torch.device(device)
-        torch.cuda.set_device(dev if dev.index is not None else torch.device("cuda", 0))
+        if dev.index is not None:   # a bare "cuda" keeps the current device (one process per GPU)
+            torch.cuda.set_device(dev)
         b = BinFile(path)
         self.shape = b.shape
         b.close()

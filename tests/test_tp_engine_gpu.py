@@ -55,12 +55,13 @@ def _run(eng, prompt, nl):
 
 
 def _rank_main(rank, world, port, path, out_q):
+    import datetime
     import torch.distributed as dist
     from atomflow_b200.decode import DecodeEngine
     from atomflow_b200.tp import TpComm
     torch.cuda.set_device(rank)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180))
     prompt = np.random.default_rng(4).integers(0, 65536, TF).tolist()
     try:
         single = None
@@ -108,10 +109,14 @@ def test_tp_engine_two_gpus(tmp_path):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(path), q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(path), q), daemon=True) for r in range(2)]
     for p in procs:
         p.start()
-    msgs = [q.get(timeout=600)]
-    for p in procs:
-        p.join(timeout=600)
-    assert msgs[0] == "ok", msgs
+    try:
+        msg = q.get(timeout=400)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():   # a rank still waiting on its peer: end it, not the run
+                p.kill()
+    assert msg == "ok", msg

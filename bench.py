@@ -554,16 +554,23 @@ def run_decode(args, device, local):
     replay per token, position and token kept on the device.  Reference: its
     own AtomFlowEngine (oracle/_ref), TPOT as its main.cu measures it -- one
     graph of forward_pass at position 1024, replayed."""
+    world = int(os.environ.get("WORLD_SIZE", "1")) if args.impl == "ours" else 1
+    rank = int(os.environ.get("RANK", "0")) if world > 1 else 0
+    if world > 1 and rank != 0:
+        torch.distributed.barrier()          # rank 0 writes the model file once
     path = decode_model_path()
-    sampler = ClockSampler(local)
-    sampler.wait_first()
+    if world > 1 and rank == 0:
+        torch.distributed.barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.wait_first()
     peak, peak_kind = measured_peaks()
     config = {"workload": "llama3.2-3b-shaped greedy decode, 28 layers, random-init weights in the reference .bin "
                           "format (BASELINE config 3)", "position": DECODE_POS, "M": 1,
               "kv_cache": f"prefilled to {DECODE_POS} positions by teacher-forced steps (seeded random tokens)",
-              "l2": "3.8 GB read per step (weights, lm_head, KV cache) >> 126 MB L2 (no flush needed)", "parallelism": "single"}
+              "l2": "3.8 GB read per step (weights, lm_head, KV cache) >> 126 MB L2 (no flush needed)", "parallelism": f"tp{world}" if world > 1 else "single"}
     out = {"metric": "decode tok/s (Llama-3.2-3B-shaped, M=1, KV cache at 1024 positions)", "unit": "tok/s",
-           "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "fp8e4m3 weights x fp16 act, fp32 accum", "data": "synthetic seeded",
            "config": config}
     if args.impl == "reference":
@@ -590,10 +597,28 @@ def run_decode(args, device, local):
         R.afref_engine_destroy(h)
         return 0
     from atomflow_b200.decode import DecodeEngine
-    eng = DecodeEngine(path, mode=args.decode_mode)
+    comm = None
+    if world > 1:
+        from atomflow_b200.tp import TpComm
+        if args.decode_mode != "fast":
+            raise SystemExit("tensor-parallel decode runs the fast mode")
+        from atomflow_b200.weights_bin import BinFile
+        b = BinFile(path)
+        comm = TpComm(rank, world, b.shape.dim)
+        b.close()
+    eng = DecodeEngine(path, mode=args.decode_mode, comm=comm)
     config["engine"] = (f"C++ af_engine, {args.decode_mode} mode: " +
                         ("every kernel bit-identical to the reference's" if args.decode_mode == "exact" else
                          "fused tensor-core projections, split-KV attention"))
+    if world > 1:
+        config["engine"] += (f"; Megatron tensor parallel over {world} GPUs: QKV/gate/up column-split, O/down "
+                             "row-split with the all-reduce and residual fused into the GEMV over NVLink peer "
+                             "memory, vocab-parallel lm_head with the argmax pairs exchanged in-kernel")
+
+    def sync_all():
+        eng.stream.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
     rng = np.random.default_rng(0)
     prompt = rng.integers(0, 65536, DECODE_POS).tolist()
     g = eng.capture(advance=True)
@@ -614,19 +639,20 @@ def run_decode(args, device, local):
         eng.replay(g)
     eng.current_pos = DECODE_POS
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    eng.stream.synchronize()
+    sync_all()
     t0 = time.time()
     ev0.record(eng.stream)
     for _ in range(args.steps):
         eng.replay(g)
     ev1.record(eng.stream)
-    eng.stream.synchronize()
+    sync_all()
     t1 = time.time()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    clocks = sampler.summary(t0, t1)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+    clocks = sampler.summary(t0, t1) if sampler else None
     # end to end: each step the host sends the token from pinned memory, the
     # captured step runs, and the next token returns to pinned memory
     cudart = ctypes.CDLL("libcudart.so.12")
+    cudart.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
     cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
     tok_h = torch.zeros(1, dtype=torch.int32).pin_memory()
     tok_back = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -641,14 +667,15 @@ def run_decode(args, device, local):
     for _ in range(3):
         e2e_step()
     eng.current_pos = DECODE_POS
-    eng.stream.synchronize()
+    sync_all()
     ev0.record(eng.stream)
     for _ in range(args.steps):
         e2e_step()
     ev1.record(eng.stream)
-    eng.stream.synchronize()
-    e2e_ms = ev0.elapsed_time(ev1) / args.steps
-    sampler.stop()
+    sync_all()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+    if sampler:
+        sampler.stop()
     # greedy tokens from position DECODE_POS, checked against the reference engine's
     eng.current_pos = DECODE_POS
     eng.inject_token(first_token)
@@ -657,20 +684,43 @@ def run_decode(args, device, local):
         eng.replay(g)
         ours_toks.append(eng.get_output_token())
     tokens = {"greedy_steps": TOKEN_CHECK_STEPS, "from_position": DECODE_POS, "ours": ours_toks}
+    if comm is not None and comm.status() != 0:
+        raise RuntimeError("tensor-parallel decode: a peer wait ran out (status word set)")
+    launches = eng.launches_per_step * args.steps
+    if world > 1:
+        sync_all()
+        eng.close()
+        if rank != 0:
+            return finish(True)
     import oracle
     R = oracle.ref_engine() if not args.no_token_check and config["kv_cache"].startswith("prefilled") else None
     if R is not None:
         h = R.afref_engine_create(str(path).encode())
         tok = None
-        ref_toks = []
+        ref_toks, margins = [], []
+        nv = ctypes.c_int(0)
         for pos in range(DECODE_POS + TOKEN_CHECK_STEPS):
             tok = R.afref_engine_step(h, int(prompt[pos]) if pos < DECODE_POS else tok, pos)
             if pos >= DECODE_POS:
                 ref_toks.append(tok)
+                # the reference's two best candidate logits (ids < 65536, as its argmax)
+                torch.cuda.synchronize()
+                src = R.afref_engine_logits(h, ctypes.byref(nv))
+                t = torch.empty(eng.V, dtype=torch.float32, device="cuda")
+                torch.cuda.synchronize()
+                cudart.cudaMemcpy(ctypes.c_void_p(t.data_ptr()), ctypes.c_void_p(src), ctypes.c_size_t(4 * eng.V), 3)
+                top = torch.topk(t[:65536], 2).values.tolist()
+                margins.append(top[0] - top[1])
         R.afref_engine_destroy(h)
         div = [i for i, (a, b) in enumerate(zip(ours_toks, ref_toks)) if a != b]
         tokens.update({"reference": ref_toks, "match_reference": not div,
                        "first_divergence": (DECODE_POS + div[0]) if div else None})
+        if div:
+            # a greedy sequence after a divergence is a different sequence: what
+            # matters is whether the first divergence is a near tie in the
+            # reference's own logits (two candidates closer than rounding)
+            tokens["reference_top2_margin_at_divergence"] = round(margins[div[0]], 6)
+            tokens["reference_min_top2_margin"] = round(min(margins), 6)
     else:
         tokens["match_reference"] = None
     step_bytes = eng.weight_bytes() + eng.kv_bytes(DECODE_POS + args.steps // 2)
@@ -682,13 +732,62 @@ def run_decode(args, device, local):
                              "traffic": None, "kernel": "whole step (GEMV kernels carry 94% of the bytes)",
                              "per_launch": f"{step_bytes / 1e9:.3f} GB per step (weights, scales, norms, lm_head, "
                                            f"embedding row, KV cache) over {ms * 1e3:.1f} us"},
-                "gpu_launches": eng.launches_per_step * args.steps, "tokens": tokens,
+                "gpu_launches": launches, "tokens": tokens,
                 "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 5),
                         "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                         "path": "af_engine (C++) over the C ABI: token H2D from pinned memory, the captured step, next "
                                 "token D2H to pinned memory, every step"}})
+    if world > 1:
+        out["roofline"]["achieved"] = round(achieved / world, 2)   # per GPU: each reads 1/world of the bytes
+        out["roofline"]["frac"] = round(achieved / world / peak, 4)
+        out["roofline"]["per_launch"] += f"; {world} GPUs, each reading about 1/{world} of it"
+    out["roofline"]["traffic"] = traffic_from_profiles("decode", 1)
+    if not args.no_cpu_baseline and world == 1:
+        out["cpu_baseline"] = decode_cpu_baseline(path)
     print(json.dumps(out))
-    return 0
+    return finish(world > 1)
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def decode_cpu_baseline(path, budget_s=15.0):
+    """The reference's GEMV arithmetic as a host loop (oracle, OpenMP over
+    rows) over the model file's own projections, layer after layer until
+    ~budget_s pass, scaled to tokens/s for the step's 28 layers of projections
+    plus the FP16 lm_head at the same bytes/s.  Attention and the small
+    elementwise kernels are left out, so this is an upper bound on the host's
+    token rate."""
+    import oracle
+    from atomflow_b200.weights_bin import BinFile
+    L = oracle.cpu()
+    L.af_oracle_gemv_cpu_baseline.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 2 + [ctypes.c_void_p, ctypes.c_int]
+    b = BinFile(path)
+    s = b.shape
+    cores = os.cpu_count() or 1
+    x = np.random.default_rng(1).standard_normal(max(s.dim, s.ffn)).astype(np.float16).view(np.uint16)
+    y = np.empty(max(s.qkv_out, s.ffn), np.uint16)
+    done_layers, nbytes, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        for name, N, K in s.linears():
+            q, sc = b.linear(done_layers % s.n_layers, name)
+            L.af_oracle_gemv_cpu_baseline(x.ctypes.data, q.ctypes.data, sc.ctypes.data, N, K, y.ctypes.data, cores)
+            nbytes += algorithmic_bytes(N, K)
+        done_layers += 1
+    dt = time.perf_counter() - t0
+    b.close()
+    rate = nbytes / dt                                   # bytes/s of the host loop
+    layer_b = sum(algorithmic_bytes(N, K) for _, N, K in s.linears())
+    step_b = layer_b * s.n_layers + s.vocab * s.dim * 2  # projections + FP16 lm_head
+    return {"value": round(rate / step_b, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{done_layers} layer passes over the model file's 28 layers x 5 projections "
+                      f"({nbytes / 1e9:.2f} GB algorithmic) in {dt:.1f} s on {cores} OpenMP threads "
+                      f"({rate / 1e9:.2f} GB/s), scaled to one step's projections + lm_head; attention excluded"}
 
 
 def main():
@@ -730,8 +829,6 @@ def main():
 
     wl = args.workload
     if wl == "decode":
-        if world > 1:
-            raise SystemExit("the decode workload runs on one GPU")
         return run_decode(args, device, local)
     if wl == "layerset":
         items = make_layerset(device, trank, tp, layers=args.layers)

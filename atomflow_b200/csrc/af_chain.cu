@@ -93,7 +93,7 @@ struct Op {
 struct Params {
     int n_ops;
     int stages;                 // ring stages
-    int x_bytes, sc_bytes;      // shared carve-up: x [K] FP16, one staged-scale buffer (two of them),
+    int x_bytes, sc_bytes;      // shared carve-up: x [K] FP16 (two of them), one staged-scale buffer (two of them),
     int sct_bytes;              // and the transposed scales of the current op
     int* counters;              // [n_ops + 1] completion counters (null: no op waits)
     unsigned long long wait_ns;
@@ -206,8 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     constexpr int kPitch = pitch<EXACT>();
     const int S = p.stages;
     unsigned char* ring = smem;
-    __half* xs = reinterpret_cast<__half*>(smem + (size_t)S * kStage);
-    unsigned char* scb = reinterpret_cast<unsigned char*>(xs) + p.x_bytes;
+    // x of op o sits in buffer o & 1: an op that does not wait for the previous
+    // one has its x fetched (cp.async) while the previous op computes
+    unsigned char* const xbase = smem + (size_t)S * kStage;
+    auto xbuf = [&](int o) { return reinterpret_cast<__half*>(xbase + (size_t)(o & 1) * p.x_bytes); };
+    unsigned char* scb = smem + (size_t)S * kStage + 2 * (size_t)p.x_bytes;
     uint16_t* sct = reinterpret_cast<uint16_t*>(scb + 2 * (size_t)p.sc_bytes);   // [m][G][rows_pad]
     __shared__ __align__(8) uint64_t full[16], empty[16], sc_full[2], sc_empty[2];
     // warp sums of the last 8 tiles: consumer warps run at most one ring (<= 6
@@ -345,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         uint32_t phase = 0;
         int tb = 0;
         bool ready = false;   // the next stage's full barrier tested complete
+        bool x_pref = false;  // this op's x was fetched during the previous op
         for (int o = 0; o < p.n_ops; ++o) {
             const Op& op = p.ops[o];
             const RowSplit rs = row_split(op);
@@ -378,11 +382,27 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
                     }
                 }
             }
+            if (x_pref) cp_async_wait<0>();   // this op's x, fetched during the previous op
             named_bar_sync(1, kCWarps * 32);
-            // x -> shared (L2-coherent loads: another CTA may have written it)
-            for (int i = ct * 8; i < K; i += kCWarps * 32 * 8)
-                *reinterpret_cast<uint4*>(xs + i) = ldcg_u4(op.x + i);
-            named_bar_sync(1, kCWarps * 32);
+            __half* xs = xbuf(o);
+            if (!x_pref) {
+                // x -> shared (L2-coherent loads: another CTA may have written it)
+                for (int i = ct * 8; i < K; i += kCWarps * 32 * 8)
+                    *reinterpret_cast<uint4*>(xs + i) = ldcg_u4(op.x + i);
+                named_bar_sync(1, kCWarps * 32);
+            }
+            // The next op's x, if that op reads nothing this one writes (it does
+            // not wait): its buffer was last read by op o - 1, which every warp
+            // has finished (the barrier at this op's start), and any op it might
+            // depend on further back finished before this op's wait above.
+            x_pref = false;
+            if (o + 1 < p.n_ops && !p.ops[o + 1].wait) {   // uniform: every thread takes the same branch
+                const Op& nx = p.ops[o + 1];
+                const uint32_t xd = smem_u32(xbuf(o + 1));
+                for (int i = ct * 8; i < nx.K; i += kCWarps * 32 * 8) cp_async16(xd + 2 * i, nx.x + i);
+                cp_async_commit();
+                x_pref = true;
+            }
             if (op.kind == OP_RMSNORM_GEMV || op.kind == OP_RMSNORM_SWIGLU) {
                 // RMSNorm of x in the reference's arithmetic (src/kernel/rmsnorm.cu:9-67,
                 // 128 threads): strided FMA sums, shuffle-down tree 1..16, the four
@@ -705,7 +725,7 @@ af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_
         if (workspace == nullptr || ws_bytes < af_chain_workspace_bytes(n_ops)) return AF_ERR_WORKSPACE;
         if (!aligned(workspace, 4)) return AF_ERR_INVALID;
     }
-    const size_t fixed = xb + 2 * scb + sctb + 6144;   // + static shared memory and alignment
+    const size_t fixed = 2 * xb + 2 * scb + sctb + 6144;   // + static shared memory and alignment
     const size_t kStage = exact ? stage_bytes<true>() : stage_bytes<false>();
     if (fixed + 2 * kStage > kSmemCap) return AF_ERR_UNSUPPORTED;
     // one projection: a 3-stage ring (two CTAs per SM, so the next kernel's CTA
@@ -751,7 +771,7 @@ af_status chain_launch(const af_chain_op* ops, int n_ops, void* workspace, size_
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sms);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = (size_t)stages * kStage + xb + 2 * scb + sctb;
+    cfg.dynamicSmemBytes = (size_t)stages * kStage + 2 * xb + 2 * scb + sctb;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     if (waits) {

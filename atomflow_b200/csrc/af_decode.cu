@@ -7,6 +7,7 @@
 // build_rope_cache, k_write_kv_cache), src/kernel/rope.cu (rope_kernel),
 // src/kernel/tiled_attention.cu:183-269 (gqa_cached_attention_kernel),
 // src/kernel/rmsnorm.cu (rms_norm_kernel); order of use src/core/engine.cu:262-521.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
@@ -360,41 +361,61 @@ __global__ void __launch_bounds__(G * 128) attention_kernel(
 }
 
 // ------------------------------------------- cached attention, fast form
-// Split-KV GQA attention for one token, within FP16 rounding of FP64 (online
-// softmax: not the reference's summation order, so not bit-identical to it).  CTA (split, kv head) handles
-// positions [t0, t1) of the cache for the G = NH/NKV query heads that share
-// the kv head; each of its 8 warps takes every 8th position with an online
-// softmax (lane l holds dims 4l..4l+3; two positions' loads in flight).  The
-// CTA's partial (max, sum, o) goes to the workspace; the last CTA of the kv
-// head merges the splits in split order (deterministic) and writes out, then
-// re-zeroes its counter.  (A lane-per-position layout -- one k row per lane,
-// then p.v by dims -- was measured slower at 1-2k positions: with 32 splits
-// a CTA has ~32 positions, which left one warp doing all of them.)
-constexpr int kAttnSplits = 32;
+// Within FP16 rounding of FP64 (online softmax: not the reference's summation
+// order, so not bit-identical to it).  One thread-block cluster per kv head.
+// The kv head's positions are cut into kClus contiguous ranges, one per CTA of
+// the cluster, and each CTA's into per-warp strided positions.  Every warp
+// issues the K/V loads of up to kClusBatch positions before it does anything
+// else with them (right after reading the position), so a CTA pays about one
+// DRAM round trip per batch; the query heads are rotated while those loads fly.
+// Each warp keeps an online softmax (running max, sum and P.V), the warps
+// merge through shared memory, and the cluster's CTAs merge their partials in
+// rank order through distributed shared memory -- no global workspace, fence
+// or counter.  Results are deterministic (fixed merge order).
+constexpr int kClus = 8;
+constexpr int kClusBatch = 16;
 
-template <int G, int kAttnWarps>
-__global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
-    const __half* __restrict__ q, const __half* __restrict__ k_cache, const __half* __restrict__ v_cache,
-    const int* __restrict__ d_pos, __half* __restrict__ out, int NKV, float* __restrict__ part,
-    int* __restrict__ counters, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
+template <int G>
+__global__ void __cluster_dims__(kClus, 1, 1) __launch_bounds__(256) attention_cluster_kernel(
+    const __half* __restrict__ q, const __half* k_cache, const __half* v_cache, const int* __restrict__ d_pos,
+    __half* __restrict__ out, int NKV, const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int NH,
     int form, __half* k_wr, __half* v_wr, int max_seq) {
-    // cos_tab != null: RoPE + KV write fused in.  q then points at the raw qkv
-    // vector: every CTA rotates its own query heads, and the current position's
-    // k (rotated) and v come from qkv in registers; the one CTA whose range
-    // holds that position also writes them to the caches (no CTA reads that row).
-    constexpr int HD = 128;
-    const int split = blockIdx.x, kvh = blockIdx.y;
+    constexpr int HD = 128, W = 8, rec = 2 + HD;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int split = (int)cluster.block_rank(), kvh = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (pos_out_of_range(*d_pos, max_seq)) return;
-    const int seq = *d_pos + 1;
-    const int chunk = (seq + kAttnSplits - 1) / kAttnSplits;
+    const int pos = *d_pos;
+    if (pos_out_of_range(pos, max_seq)) return;   // every CTA of the cluster reads the same d_pos
+    const int seq = pos + 1;
+    const int chunk = (seq + kClus - 1) / kClus;
     const int t0 = min(seq, split * chunk), t1 = min(seq, t0 + chunk);
     const int kv_dim = NKV * HD;
-    const float scale = rsqrtf((float)HD);   // as the reference (tiled_attention.cu:202)
-
+    const size_t col = (size_t)kvh * HD + lane * 4;
     const bool fused = cos_tab != nullptr;
-    const int pos = seq - 1;
-    // RoPE of 4 dims held by this lane; dims d and d + HD/2 sit in lanes l and l ^ 16.
+
+    uint2 kr[kClusBatch], vr[kClusBatch];
+    auto fetch = [&](int tb) {
+#pragma unroll
+        for (int i = 0; i < kClusBatch; ++i) {
+            const int t = tb + warp + i * W;
+            if (t < t1 && !(fused && t == pos)) {
+                kr[i] = *reinterpret_cast<const uint2*>(k_cache + (size_t)t * kv_dim + col);
+                vr[i] = *reinterpret_cast<const uint2*>(v_cache + (size_t)t * kv_dim + col);
+            } else {
+                kr[i] = vr[i] = make_uint2(0u, 0u);
+            }
+        }
+    };
+    fetch(t0);
+
+    auto unpack4 = [](const uint2 raw, float (&v)[4]) {
+        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
+        v[0] = __low2float(a);
+        v[1] = __high2float(a);
+        v[2] = __low2float(b);
+        v[3] = __high2float(b);
+    };
     float rc[4], rs[4];
     if (fused) {
 #pragma unroll
@@ -409,34 +430,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
         for (int e = 0; e < 4; ++e) {
             const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
             float o0, o1;
-            // (x, y) = (dim d, dim d + HD/2): lanes < 16 own x and keep o0, the others own y and keep o1
             if (lane < 16) rope_pair(v[e], other, rc[e], rs[e], form, o0, o1);
             else rope_pair(other, v[e], rc[e], rs[e], form, o0, o1);
             v[e] = __half2float(__float2half_rn(lane < 16 ? o0 : o1));
         }
     };
-    auto load4 = [&](const __half* src, float (&v)[4]) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(src);
-        const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
-        v[0] = __low2float(a);
-        v[1] = __high2float(a);
-        v[2] = __low2float(b);
-        v[3] = __high2float(b);
-    };
     float qv[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        load4(q + (size_t)(kvh * G + g) * HD + lane * 4, qv[g]);
+        unpack4(*reinterpret_cast<const uint2*>(q + (size_t)(kvh * G + g) * HD + lane * 4), qv[g]);
         if (fused) rotate(qv[g]);
     }
-    float kcur[4], vcur[4];
+    float kcur[4] = {0.f, 0.f, 0.f, 0.f}, vcur[4] = {0.f, 0.f, 0.f, 0.f};
     if (fused) {
         const __half* kq = q + (size_t)NH * HD + (size_t)kvh * HD + lane * 4;
-        load4(kq, kcur);
+        unpack4(*reinterpret_cast<const uint2*>(kq), kcur);
         rotate(kcur);
-        load4(kq + (size_t)NKV * HD, vcur);
-        if (warp == 0 && t0 <= pos && pos < t1) {
-            const size_t row = (size_t)pos * kv_dim + (size_t)kvh * HD + lane * 4;
+        unpack4(*reinterpret_cast<const uint2*>(kq + (size_t)NKV * HD), vcur);
+        if (warp == 0 && t0 <= pos && pos < t1) {   // this CTA's range holds the new row: store it
+            const size_t row = (size_t)pos * kv_dim + col;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 k_wr[row + e] = __float2half_rn(kcur[e]);
@@ -444,6 +456,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
             }
         }
     }
+    const float scale = rsqrtf((float)HD);
     float m[G], l[G], o[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -451,64 +464,46 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
         l[g] = 0.f;
         o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
     }
-    auto load = [&](int t, float (&kf)[4], float (&vf)[4]) {
-        if (fused && t == pos) {
+    for (int tb = t0; tb < t1; tb += kClusBatch * W) {
+        if (tb != t0) fetch(tb);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                kf[e] = kcur[e];
-                vf[e] = vcur[e];
+        for (int i = 0; i < kClusBatch; ++i) {
+            const int t = tb + warp + i * W;
+            if (t >= t1) break;
+            float kf[4], vf[4];
+            if (fused && t == pos) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    kf[e] = kcur[e];
+                    vf[e] = vcur[e];
+                }
+            } else {
+                unpack4(kr[i], kf);
+                unpack4(vr[i], vf);
             }
-            return;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float sdot = qv[g][0] * kf[0];
+                sdot = fmaf(qv[g][1], kf[1], sdot);
+                sdot = fmaf(qv[g][2], kf[2], sdot);
+                sdot = fmaf(qv[g][3], kf[3], sdot);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+                const float sc = sdot * scale;
+                const float mn = fmaxf(m[g], sc);
+                const float corr = __expf(m[g] - mn);   // 0 on the first position (m = -inf)
+                const float pw = __expf(sc - mn);
+                l[g] = l[g] * corr + pw;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
+                m[g] = mn;
+            }
         }
-        const size_t row = (size_t)t * kv_dim + (size_t)kvh * HD + lane * 4;
-        const uint2 kr = *reinterpret_cast<const uint2*>(k_cache + row);
-        const uint2 vr = *reinterpret_cast<const uint2*>(v_cache + row);
-        const __half2 k0 = *reinterpret_cast<const __half2*>(&kr.x), k1 = *reinterpret_cast<const __half2*>(&kr.y);
-        const __half2 v0 = *reinterpret_cast<const __half2*>(&vr.x), v1 = *reinterpret_cast<const __half2*>(&vr.y);
-        kf[0] = __low2float(k0);
-        kf[1] = __high2float(k0);
-        kf[2] = __low2float(k1);
-        kf[3] = __high2float(k1);
-        vf[0] = __low2float(v0);
-        vf[1] = __high2float(v0);
-        vf[2] = __low2float(v1);
-        vf[3] = __high2float(v1);
-    };
-    auto consume = [&](const float (&kf)[4], const float (&vf)[4]) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            float sdot = qv[g][0] * kf[0];
-            sdot = fmaf(qv[g][1], kf[1], sdot);
-            sdot = fmaf(qv[g][2], kf[2], sdot);
-            sdot = fmaf(qv[g][3], kf[3], sdot);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
-            const float sc = sdot * scale;
-            const float mn = fmaxf(m[g], sc);
-            const float corr = __expf(m[g] - mn);   // 0 on the first position (m = -inf)
-            const float pw = __expf(sc - mn);
-            l[g] = l[g] * corr + pw;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][e] = fmaf(pw, vf[e], o[g][e] * corr);
-            m[g] = mn;
-        }
-    };
-    int t = t0 + warp;
-    for (; t + kAttnWarps < t1; t += 2 * kAttnWarps) {
-        float ka[4], va[4], kb[4], vb[4];
-        load(t, ka, va);
-        load(t + kAttnWarps, kb, vb);
-        consume(ka, va);
-        consume(kb, vb);
     }
-    if (t < t1) {
-        float ka[4], va[4];
-        load(t, ka, va);
-        consume(ka, va);
-    }
-    // merge the 4 warps through shared memory, then this CTA's partial to the workspace
-    __shared__ float s_m[kAttnWarps][G], s_l[kAttnWarps][G];
-    __shared__ float s_o[kAttnWarps][G][HD];
+    // the warps' partials -> this CTA's partial (m, l, o[HD]) per query head
+    __shared__ float s_m[W][G], s_l[W][G];
+    __shared__ float s_o[W][G][HD];
+    __shared__ float s_part[G * rec];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         if (lane == 0) {
@@ -519,59 +514,53 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_split_kernel(
         for (int e = 0; e < 4; ++e) s_o[warp][g][lane * 4 + e] = o[g][e];
     }
     __syncthreads();
-    constexpr int rec = 2 + HD;   // (m, l, o[HD]) per query head
-    float* my = part + ((size_t)kvh * kAttnSplits + split) * G * rec;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float mm = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) mm = fmaxf(mm, s_m[w][g]);
+        for (int w = 0; w < W; ++w) mm = fmaxf(mm, s_m[w][g]);
         float ll = 0.f, oo = 0.f;
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
+        for (int w = 0; w < W; ++w) {
             const float f = s_m[w][g] == -INFINITY ? 0.f : __expf(s_m[w][g] - mm);
             ll = fmaf(s_l[w][g], f, ll);
             oo = fmaf(s_o[w][g][d], f, oo);
         }
-        __stcg(my + g * rec + 2 + d, oo);
+        s_part[g * rec + 2 + d] = oo;
         if (d == 0) {
-            __stcg(my + g * rec, mm);
-            __stcg(my + g * rec + 1, ll);
+            s_part[g * rec] = mm;
+            s_part[g * rec + 1] = ll;
         }
     }
-    __threadfence();
-    __syncthreads();
-    __shared__ int s_last;
-    if (threadIdx.x == 0) s_last = atomicAdd(counters + kvh, 1) == kAttnSplits - 1;
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const float* all = part + (size_t)kvh * kAttnSplits * G * rec;
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int g = i / HD, d = i % HD;
-        float ms[kAttnSplits], ls[kAttnSplits], os[kAttnSplits];
+    cluster.sync();   // every CTA's partial is visible to the cluster
+    if (split == 0) {
+        const float* parts[kClus];
 #pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) {   // independent loads, all in flight
-            const float* r = all + (size_t)sp * G * rec + g * rec;
-            ms[sp] = ldcg_f32(r);
-            ls[sp] = ldcg_f32(r + 1);
-            os[sp] = ldcg_f32(r + 2 + d);
+        for (int r = 0; r < kClus; ++r) parts[r] = cluster.map_shared_rank(s_part, r);
+        for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+            const int g = i / HD, d = i % HD;
+            float ms[kClus], ls[kClus], os[kClus];
+#pragma unroll
+            for (int r = 0; r < kClus; ++r) {
+                ms[r] = parts[r][g * rec];
+                ls[r] = parts[r][g * rec + 1];
+                os[r] = parts[r][g * rec + 2 + d];
+            }
+            float mm = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kClus; ++r) mm = fmaxf(mm, ms[r]);
+            float ll = 0.f, oo = 0.f;
+#pragma unroll
+            for (int r = 0; r < kClus; ++r) {   // rank order: deterministic
+                const float f = ms[r] == -INFINITY ? 0.f : __expf(ms[r] - mm);   // empty ranges add nothing
+                ll = fmaf(ls[r], f, ll);
+                oo = fmaf(os[r], f, oo);
+            }
+            out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
         }
-        float mm = -INFINITY;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) mm = fmaxf(mm, ms[sp]);
-        float ll = 0.f, oo = 0.f;
-#pragma unroll
-        for (int sp = 0; sp < kAttnSplits; ++sp) {   // split order: deterministic
-            const float f = ms[sp] == -INFINITY ? 0.f : __expf(ms[sp] - mm);   // empty splits add nothing
-            ll = fmaf(ls[sp], f, ll);
-            oo = fmaf(os[sp], f, oo);
-        }
-        out[(size_t)(kvh * G + g) * HD + d] = __float2half_rn(oo / ll);
     }
-    if (threadIdx.x == 0) counters[kvh] = 0;   // leave the workspace counter at zero
+    cluster.sync();   // no CTA leaves while rank 0 still reads its shared memory
 }
-
 
 // ------------------------------------------------------------- RMSNorm
 // The reference's rms_norm_kernel<half, 128> arithmetic (rmsnorm.cu:9-67):
@@ -641,10 +630,8 @@ extern "C" af_status af_rope_kv_write(void* qkv, const float* cos_tab, const flo
 
 extern "C" size_t af_decode_attention_workspace_bytes(int n_heads, int n_kv_heads, int max_seq) {
     if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads || max_seq <= 0) return 0;
-    // the exact form's scores [NH][max_seq], or the fast form's split partials, whichever is larger
-    const size_t g = n_heads / n_kv_heads;
-    const size_t exact = (size_t)n_heads * max_seq * 4, fast = (size_t)n_kv_heads * kAttnSplits * g * (2 + 128) * 4;
-    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (exact > fast ? exact : fast);
+    // the exact form's scores [NH][max_seq] (the fast form needs none)
+    return 256 + round_up((size_t)n_kv_heads * 4, 256) + (size_t)n_heads * max_seq * 4;
 }
 
 static af_status attention_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
@@ -694,7 +681,7 @@ static af_status attention_launch(const void* q, const void* k_cache, const void
     return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_kernel");
 }
 
-static af_status attention_split_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
+static af_status attention_fast_launch(const void* q, const void* k_cache, const void* v_cache, const int* d_pos,
                                         void* out, int n_heads, int n_kv_heads, int head_dim, int max_seq,
                                         void* workspace, size_t workspace_bytes, void* stream, const float* cos_tab,
                                         const float* sin_tab) {
@@ -704,31 +691,26 @@ static af_status attention_split_launch(const void* q, const void* k_cache, cons
         return AF_ERR_INVALID;
     if (head_dim != 128 || n_heads / n_kv_heads > kAttnMaxG) return AF_ERR_UNSUPPORTED;
     if (!aligned(q, 8) || !aligned(k_cache, 8) || !aligned(v_cache, 8) || !aligned(out, 2)) return AF_ERR_INVALID;
-    const size_t need = af_decode_attention_workspace_bytes(n_heads, n_kv_heads, max_seq);
-    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) return AF_ERR_WORKSPACE;
-    unsigned char* ws = static_cast<unsigned char*>(workspace);
-    int* counters = reinterpret_cast<int*>(ws + 256);
-    float* part = reinterpret_cast<float*>(ws + 256 + round_up((size_t)n_kv_heads * 4, 256));
-    constexpr int warps = 8;
-    const dim3 grid(kAttnSplits, n_kv_heads), block(warps * 32);
+    (void)workspace;   // the cluster form merges in distributed shared memory: no workspace
+    (void)workspace_bytes;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     const __half *qh = static_cast<const __half*>(q), *kh = static_cast<const __half*>(k_cache),
                  *vh = static_cast<const __half*>(v_cache);
     __half* oh = static_cast<__half*>(out);
     __half* kw = cos_tab ? const_cast<__half*>(kh) : nullptr;
     __half* vw = cos_tab ? const_cast<__half*>(vh) : nullptr;
+    const dim3 cgrid(kClus, n_kv_heads);
     switch (n_heads / n_kv_heads) {
-#define AF_ATTN(GG) \
+#define AF_ATTN(GG)                                                                                            \
     case GG:                                                                                                  \
-        attention_split_kernel<GG, warps><<<grid, block, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, part,      \
-                                                                  counters, cos_tab, sin_tab, n_heads, kRopeForm, \
-                                                                  kw, vw, max_seq);                            \
+        attention_cluster_kernel<GG><<<cgrid, 256, 0, cs>>>(qh, kh, vh, d_pos, oh, n_kv_heads, cos_tab, sin_tab, \
+                                                            n_heads, kRopeForm, kw, vw, max_seq);             \
         break;
         AF_ATTN(1) AF_ATTN(2) AF_ATTN(3) AF_ATTN(4) AF_ATTN(5) AF_ATTN(6) AF_ATTN(7) AF_ATTN(8)
 #undef AF_ATTN
     }
     cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_split_kernel");
+    return e == cudaSuccess ? AF_OK : cuda_fail(e, "attention_cluster_kernel");
 }
 
 extern "C" af_status af_decode_rope_attention_fast(void* qkv, const float* cos_tab, const float* sin_tab,
@@ -736,7 +718,7 @@ extern "C" af_status af_decode_rope_attention_fast(void* qkv, const float* cos_t
                                                   int n_heads, int n_kv_heads, int head_dim, int max_seq,
                                                   void* workspace, size_t workspace_bytes, void* stream) {
     if (cos_tab == nullptr || sin_tab == nullptr) return AF_ERR_INVALID;
-    return attention_split_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, max_seq,
+    return attention_fast_launch(qkv, k_cache, v_cache, d_pos, out, n_heads, n_kv_heads, head_dim, max_seq,
                                   workspace, workspace_bytes, stream, cos_tab, sin_tab);
 }
 

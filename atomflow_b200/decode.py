@@ -10,7 +10,7 @@ for tests and the benchmark.
 Modes: "exact" -- every kernel bit-identical to the reference's (projection
 chains, attention, norms, RoPE, SwiGLU, residual, embedding; the lm_head is
 the library's, the reference's is a cuBLAS call); "fast" -- fused tensor-core
-projections and split-KV attention, within FP16 rounding of FP64.  The
+projections and cluster attention, within FP16 rounding of FP64.  The
 argmax is the reference's (ids < 65536, its launch_argmax behaviour) unless
 `true_argmax` is set.
 """

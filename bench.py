@@ -609,7 +609,7 @@ def run_decode(args, device, local):
     eng = DecodeEngine(path, mode=args.decode_mode, comm=comm)
     config["engine"] = (f"C++ af_engine, {args.decode_mode} mode: " +
                         ("every kernel bit-identical to the reference's" if args.decode_mode == "exact" else
-                         "fused tensor-core projections, split-KV attention"))
+                         "fused tensor-core projections, cluster attention (one 8-CTA cluster per kv head)"))
     if world > 1:
         config["engine"] += (f"; Megatron tensor parallel over {world} GPUs: QKV/gate/up column-split, O/down "
                              "row-split with the all-reduce and residual fused into the GEMV over NVLink peer "
@@ -803,6 +803,9 @@ def main():
                     help="chain: tensor-core dot products (fast) or the reference kernel's FP32 FMA order (exact)")
     ap.add_argument("--launch", choices=["chain", "per-gemv"], default="per-gemv",
                     help="one-token GEMVs on one GPU: one persistent launch per step (chain) or one launch per GEMV")
+    ap.add_argument("--order", choices=["dependent", "independent"], default="dependent",
+                    help="layer set as one chain launch: each GEMV waits for the previous one (dependent, the "
+                         "order of the reference's launches) or not (independent: the layer set's GEMVs share no data)")
     ap.add_argument("--decode-mode", choices=["exact", "fast"], default="fast",
                     help="decode: kernels bit-identical to the reference's (exact) or the fused fast forms")
     ap.add_argument("--no-token-check", action="store_true",
@@ -879,13 +882,15 @@ def main():
                  all(it["x"].shape[0] == 1 for it in items if not chain))
     exact = args.math == "exact"
     if use_chain:
-        config["launch"] = "one persistent launch per step, every GEMV waits for the previous one"
+        config["launch"] = ("one persistent launch per step, every GEMV waits for the previous one"
+                            if args.order == "dependent" or chain else
+                            "one persistent launch per step over the 140 independent GEMVs (no waits between them)")
         config["math"] = ("exact: the reference kernel's FP32 FMA order, bit-identical" if exact else
                           "fast: tensor-core MMAs, FP32 accumulation, within FP16 rounding of FP64")
     if chain:
         arm = OursChain(cbufs, as_chain=use_chain, exact=exact) if args.impl == "ours" else None
     elif use_chain:
-        arm = OursChainSet(items, device, exact=exact)
+        arm = OursChainSet(items, device, wait=args.order == "dependent", exact=exact)
     else:
         arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
     if args.impl == "reference":

@@ -226,9 +226,12 @@ af_status af_decode_attention(const void* q, const void* k_cache, const void* v_
 af_status af_decode_rope_attention(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                    void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
                                    int head_dim, int max_seq, void* workspace, size_t workspace_bytes, void* stream);
-/* The same step as af_decode_rope_attention (and the same workspace) with a
- * split-KV online softmax: every output within 2 FP16 ulp / 2e-3 relative of
- * FP64, not the reference's summation order.  A fast form for throughput. */
+/* The same step as af_decode_rope_attention with an online softmax split over
+ * one 8-CTA thread-block cluster per kv head (partials merged in distributed
+ * shared memory): the KV-cache rows written are bit-identical, every output is
+ * within 2 FP16 ulp / 2e-3 relative of FP64, not the reference's summation
+ * order.  A fast form for throughput; it uses no workspace (the arguments are
+ * accepted and ignored). */
 af_status af_decode_rope_attention_fast(void* qkv, const float* cos_tab, const float* sin_tab, const int* d_pos,
                                         void* k_cache, void* v_cache, void* out, int n_heads, int n_kv_heads,
                                         int head_dim, int max_seq, void* workspace, size_t workspace_bytes,
@@ -310,7 +313,7 @@ af_status af_gemv_chain_fast(const af_chain_op* ops, int n_ops, void* workspace,
  *                    chains (af_gemv_chain), attention, norms, SwiGLU,
  *                    residual, RoPE, embedding; lm_head + argmax as
  *                    af_lm_head_gemv (the reference's is a cuBLAS call)
- *   AF_ENGINE_FAST   the fused tensor-core projections and the split-KV
+ *   AF_ENGINE_FAST   the fused tensor-core projections and the cluster
  *                    attention (af_decode_rope_attention_fast)
  * argmax_mode: AF_ARGMAX_REF_COMPAT (the reference's ids < 65536) or TRUE.
  * One engine per host thread at a time; calls are ordered on its stream. */

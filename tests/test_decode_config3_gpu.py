@@ -7,7 +7,7 @@ token ids), then 64 greedy steps from position 1024, in three engines:
   (b) the same unmodified engine.cu linked against this library, whose View
       launchers replace the reference's launch_w8a16_gemv and launch_argmax
       (oracle/_ref/libafref_engine_shim.so -- the drop-in as a user gets it);
-  (c) this library's DecodeEngine (fused projections, split-KV attention).
+  (c) this library's DecodeEngine (fused projections, cluster attention).
 
 The 64 greedy tokens must be identical in all three.  The 1024 teacher-forced
 argmaxes must agree wherever the reference's top-2 logit margin is not within

@@ -187,6 +187,62 @@ def test_fused_rope_attention_equals_the_two_kernels():
         assert torch.equal(b, qkv)   # the fused kernel leaves qkv unrotated
 
 
+def _attention_f64_g(q, kc, vc, seq, nh, nkv):
+    qf = q.cpu().double().numpy().reshape(nh, HD)
+    k = kc[:seq].cpu().double().numpy().reshape(seq, nkv, HD)
+    v = vc[:seq].cpu().double().numpy().reshape(seq, nkv, HD)
+    out = np.empty((nh, HD))
+    for h in range(nh):
+        kv = h // (nh // nkv)
+        s = k[:, kv, :] @ qf[h] / np.sqrt(HD)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        out[h] = p @ v[:, kv, :]
+    return out.ravel()
+
+
+@pytest.mark.parametrize("nh,nkv", [(24, 8), (32, 8), (8, 8), (16, 2), (12, 4)])
+def test_fast_rope_attention(nh, nkv):
+    """af_decode_rope_attention_fast (one thread-block cluster per kv head):
+    the KV-cache rows it writes are bit-identical to the exact RoPE kernel's,
+    its output is within FP16 rounding of an FP64 softmax over the same rotated
+    q and caches, and two calls in a row give the same bits."""
+    L = lib()
+    cos, sin = _tables()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(23 + nh + nkv)
+    qd, kvd = nh * HD, nkv * HD
+    ws = torch.zeros(L.af_decode_attention_workspace_bytes(nh, nkv, MAXSEQ), dtype=torch.uint8, device="cuda")
+    kc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
+    vc = torch.randn(MAXSEQ, kvd, generator=g, device="cuda").half()
+    for pos in (0, 1, 7, 33, 130, 1024, MAXSEQ - 1):
+        qkv = (torch.randn(qd + 2 * kvd, generator=g, device="cuda") * 2).half()
+        dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        ka, va = kc.clone(), vc.clone()
+        a = qkv.clone()
+        assert L.af_rope_kv_write(a.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(), ka.data_ptr(),
+                                  va.data_ptr(), nh, nkv, HD, MAXSEQ, st()) == 0
+        outs = []
+        for _ in range(2):
+            kb, vb = kc.clone(), vc.clone()
+            b = qkv.clone()
+            ob = torch.zeros(qd, dtype=torch.float16, device="cuda")
+            assert L.af_decode_rope_attention_fast(b.data_ptr(), cos.data_ptr(), sin.data_ptr(), dpos.data_ptr(),
+                                                   kb.data_ptr(), vb.data_ptr(), ob.data_ptr(), nh, nkv, HD, MAXSEQ,
+                                                   ws.data_ptr(), ws.numel(), st()) == 0
+            torch.cuda.synchronize()
+            assert torch.equal(ka.view(torch.int16), kb.view(torch.int16)), pos
+            assert torch.equal(va.view(torch.int16), vb.view(torch.int16)), pos
+            assert torch.equal(b, qkv)
+            outs.append(ob)
+        assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16)), pos
+        want = _attention_f64_g(a[:qd], ka, va, pos + 1, nh, nkv)
+        y = outs[0].float().cpu().numpy().astype(np.float64)
+        err = np.abs(y - want)
+        ok = (err <= 2 * half_ulp(want)) | (err <= 2e-3 * np.abs(want)) | (err <= 1e-4)
+        assert ok.all(), f"pos {pos}: {int((~ok).sum())} outputs off, max err {err.max():.3g}"
+
+
 def test_position_outside_the_cache_is_skipped_and_flagged():
     """A device-side position at or past max_seq (a replayed step that ran past
     the cache) must write nothing and set AF_FAULT_POSITION, not write out of

@@ -801,9 +801,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--math", choices=["fast", "exact"], default="fast",
                     help="chain: tensor-core dot products (fast) or the reference kernel's FP32 FMA order (exact)")
-    ap.add_argument("--launch", choices=["chain", "per-gemv"], default="per-gemv",
-                    help="one-token GEMVs on one GPU: one persistent launch per step (chain) or one launch per GEMV")
-    ap.add_argument("--order", choices=["dependent", "independent"], default="dependent",
+    ap.add_argument("--launch", choices=["chain", "per-gemv"], default=None,
+                    help="one-token GEMVs on one GPU: one persistent launch per step (chain; default for the "
+                         "layer set) or one launch per GEMV (per-gemv; default elsewhere)")
+    ap.add_argument("--order", choices=["dependent", "independent"], default="independent",
                     help="layer set as one chain launch: each GEMV waits for the previous one (dependent, the "
                          "order of the reference's launches) or not (independent: the layer set's GEMVs share no data)")
     ap.add_argument("--decode-mode", choices=["exact", "fast"], default="fast",
@@ -878,6 +879,8 @@ def main():
     lm = wl.startswith("lmhead")
     chain = wl == "layerchain"
     # one token per GEMV on one GPU: the whole step as one persistent launch (af_gemv_chain)
+    if args.launch is None:
+        args.launch = "chain" if wl == "layerset" else "per-gemv"
     use_chain = (args.impl == "ours" and tp == 1 and not lm and args.launch == "chain" and
                  all(it["x"].shape[0] == 1 for it in items if not chain))
     exact = args.math == "exact"
@@ -928,6 +931,16 @@ def main():
     clocks = sampler.summary(t0, t1) if sampler else None
     ms_step = ms / args.steps
     value = total_bytes / (ms_step / 1e3) / 1e9
+    if use_chain and not chain:
+        # the same GEMVs as one launch each (the reference's launch pattern), for comparison
+        gp = capture_step(OursGemv(items, device), items, stream)
+        pms, _, _ = time_graph(gp, stream, args.steps, args.warmup, dist_on)
+        gp = None
+        pv = total_bytes / (pms / args.steps / 1e3) / 1e9
+        peak_pg, _ = measured_peaks()
+        config["per_gemv_launch"] = {"value": round(pv, 2), "unit": "GB/s", "ms_per_step": round(pms / args.steps, 5),
+                                     "frac": round(pv / peak_pg, 4),
+                                     "kernel": "gemv_fp8_m1_kernel, one launch per GEMV (af_w8a16_gemv)"}
     if use_chain:
         launches = args.steps            # one persistent launch per step
     else:
@@ -1021,7 +1034,8 @@ def main():
         "roofline": {"bound": "hbm", "achieved": round(per_rank_gbs, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(per_rank_gbs / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "traffic": traffic_from_profiles(wl, len(items)) if args.impl == "ours" else None,
+                     "traffic": traffic_from_profiles("layerset_chain" if use_chain and wl == "layerset" else wl, len(items))
+                     if args.impl == "ours" else None,
                      "kernel": ({"ours": "gemv_stream_kernel (FP16 W) / gemv_fp8_m1_kernel (FP8 W)",
                                  "reference": "cublasGemmEx + argmax (reference)"} if lm else
                                 {"ours": f"chain_kernel<{'exact' if exact else 'fast'}> (one persistent launch per step)" if use_chain

@@ -70,6 +70,7 @@ C_SYMBOLS = {
     "af_workspace_reset": (_i, [_vp, _sz, _vp]),
     "af_w8a16_gemv_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "af_w8a16_gemv": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "af_w8a16_gemm_tc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
     "af_lm_head_workspace_bytes": (_sz, [_i, _i, _i]),
     "af_lm_head_gemv": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _vp, _i, _vp, _sz, _vp]),
     "af_argmax_workspace_bytes": (_sz, [_i]),

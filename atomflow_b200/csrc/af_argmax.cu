@@ -158,9 +158,10 @@ extern "C" int af_version(void) { return 110; }
 
 extern "C" af_status af_device_faults(unsigned* out, int clear) {
     if (out == nullptr) return AF_ERR_INVALID;
-    cudaError_t e1 = cudaSuccess, e2 = cudaSuccess, e3 = cudaSuccess;
-    const unsigned v = gemv_faults(clear != 0, &e1) | decode_faults(clear != 0, &e2) | chain_faults(clear != 0, &e3);
-    for (cudaError_t e : {e1, e2, e3})
+    cudaError_t e1 = cudaSuccess, e2 = cudaSuccess, e3 = cudaSuccess, e4 = cudaSuccess;
+    const unsigned v = gemv_faults(clear != 0, &e1) | decode_faults(clear != 0, &e2) | chain_faults(clear != 0, &e3) |
+                       tc_faults(clear != 0, &e4);
+    for (cudaError_t e : {e1, e2, e3, e4})
         if (e != cudaSuccess) return cuda_fail(e, "af_device_faults");
     *out = v;
     return AF_OK;

@@ -25,6 +25,11 @@ constexpr int ctas_per_sm() { return 1; }
 unsigned gemv_faults(bool clear, cudaError_t* err);
 unsigned decode_faults(bool clear, cudaError_t* err);
 unsigned chain_faults(bool clear, cudaError_t* err);
+unsigned tc_faults(bool clear, cudaError_t* err);
+// 8+ token FP8 projections on the tcgen05 tensor cores (af_gemv_tc.cu)
+bool tc_ok(int M, int K, bool row_scale, const void* x, const void* w, const void* s, const void* y);
+af_status tc_launch(const void* x, const void* w, const void* s, bool row_scale, void* y, int M, int N, int K,
+                    cudaStream_t st);
 
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

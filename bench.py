@@ -362,6 +362,17 @@ class OursGemv:
             raise RuntimeError(f"af_w8a16_gemv: {self.L.af_status_string(rc).decode()}")
 
 
+class OursGemmTc(OursGemv):
+    """The batched projection through af_w8a16_gemm_tc (tcgen05 tensor cores)."""
+
+    def launch(self, stream, it, xptr=None, yptr=None):
+        rc = self.L.af_w8a16_gemm_tc(xptr or it["x"].data_ptr(), it["q"].data_ptr(), it["s"].data_ptr(),
+                                     yptr or it["y"].data_ptr(), it["x"].shape[0], it["N"], it["K"], 128, 0,
+                                     stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"af_w8a16_gemm_tc: {self.L.af_status_string(rc).decode()}")
+
+
 class OursChainSet:
     """The layer set as ONE persistent launch (af_gemv_chain): every GEMV of the
     step in order, each waiting for the previous one to finish on every CTA --
@@ -859,12 +870,13 @@ def main():
                   "scales": "fp16 per 128-group (reference format)", "layers": args.layers,
                   "l2": "inputs 2.8 GB >> 126 MB L2 (no flush needed)",
                   "parallelism": f"tp{tp}" if tp > 1 else "single"}
-    elif wl.startswith("gemv:"):
+    elif wl.startswith("gemv:") or wl.startswith("gemmtc:"):
         parts = [int(v) for v in wl.split(":")[1:]]
         N, K = parts[0], parts[1]
         M = parts[2] if len(parts) > 2 else 1
         items = make_single(device, N, K, M)
-        config = {"workload": f"single GEMV {N}x{K} M={M}", "M": M, "copies": len(items),
+        config = {"workload": f"single GEMV {N}x{K} M={M}" + (" (af_w8a16_gemm_tc)" if wl.startswith("gemmtc") else ""),
+                  "M": M, "copies": len(items),
                   "l2": f"{len(items)} rotating weight copies ({len(items) * N * K / 1e6:.0f} MB) > 4x L2",
                   "parallelism": "single"}
     elif wl in ("lmhead:f16", "lmhead:fp8"):
@@ -895,7 +907,8 @@ def main():
     elif use_chain:
         arm = OursChainSet(items, device, wait=args.order == "dependent", exact=exact)
     else:
-        arm = (OursLmHead(items, device) if lm else OursGemv(items, device)) if args.impl == "ours" else None
+        arm = ((OursLmHead(items, device) if lm else OursGemmTc(items, device) if wl.startswith("gemmtc") else
+                OursGemv(items, device)) if args.impl == "ours" else None)
     if args.impl == "reference":
         try:
             if lm and wl.endswith("fp8"):

@@ -58,7 +58,8 @@ typedef enum af_argmax_mode {
 typedef enum af_fault_bits {
     AF_FAULT_X_COPY = 1,      /* a GEMV's bounded wait for its x copy ran out (that y is invalid) */
     AF_FAULT_POSITION = 2,    /* a decode kernel read a position outside [0, max_seq) and skipped its work */
-    AF_FAULT_CHAIN_WAIT = 4   /* a projection chain's bounded wait ran out (that launch's outputs are invalid) */
+    AF_FAULT_CHAIN_WAIT = 4,  /* a projection chain's bounded wait ran out (that launch's outputs are invalid) */
+    AF_FAULT_TC_WAIT = 8      /* an af_w8a16_gemm_tc bounded wait ran out (its outputs are invalid) */
 } af_fault_bits;
 
 const char* af_status_string(af_status s);
@@ -92,6 +93,21 @@ size_t af_w8a16_gemv_workspace_bytes(int M, int N, int K, af_scale_kind kind);
 af_status af_w8a16_gemv(const void* x, const void* w, const void* scales, void* y,
                         int M, int N, int K, int group_size, af_scale_kind kind,
                         void* workspace, size_t workspace_bytes, void* stream);
+/* The same projection for any M on the tcgen05 tensor cores (the batched /
+ * prefill shape that launch_linear_gemm declares, include/ops/kernel.h:53-59,
+ * with the reference's scales; its kernel is single-token only,
+ * src/kernel/qkv_gemm.cu:32-150).  128 weight rows form the MMA's M and 16
+ * tokens its N; FP8 is widened to FP16 in shared memory and each K=16 MMA
+ * accumulates from zero in its own TMEM block, the group scale applied to each
+ * 128-position partial sum; the CTAs that split one row tile's K form a
+ * thread-block cluster and merge in distributed shared memory (no workspace,
+ * no allocation).  FP8 group (group_size 128) or FP32 row scales, K % 128 == 0,
+ * 16-byte aligned x and w.  Within FP16 rounding of FP64, deterministic.  Its
+ * throughput is bounded by the FP8 -> FP16 widening (about 1 TB/s at M = 8 to
+ * 16), below af_w8a16_gemv's tokens-in-MMA-columns path, which therefore stays
+ * the default. */
+af_status af_w8a16_gemm_tc(const void* x, const void* w, const void* scales, void* y, int M, int N, int K,
+                           int group_size, af_scale_kind kind, void* stream);
 
 /* ------------------------------------------------------------ lm_head ---
  * logits[v] = sum_d W[v, d] * x[d]  (FP32 out, one token), optionally

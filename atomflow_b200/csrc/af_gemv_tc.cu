@@ -1,6 +1,7 @@
-// af_gemv_tc.cu -- the W8A16 projection for 8 or more tokens on the tcgen05
-// tensor cores (the batched / prefill-sized path of launch_w8a16_gemv, whose
-// reference kernel handles one token per launch: src/kernel/qkv_gemm.cu:32-150).
+// af_gemv_tc.cu -- the W8A16 projection for any number of tokens on the tcgen05
+// tensor cores (af_w8a16_gemm_tc: the batched shape launch_linear_gemm declares,
+// include/ops/kernel.h:53-59, with the reference's scales; the reference kernel
+// handles one token per launch: src/kernel/qkv_gemm.cu:32-150).
 //
 // Swap-AB: 128 weight rows form the MMA's M, 16 tokens its N, and the
 // FP32 accumulators live in tensor memory (TMEM).

@@ -15,11 +15,15 @@ import pytest
 
 import oracle
 from tests._util import assert_fp16_parity as _parity, make_gemv_case
+from tests.test_gemv_gpu import dev, gemv_np, lib
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
 
 
 def assert_fp16_parity(*a, **k):
     return _parity(*a, noise_ulps=8, **k)
-from tests.test_gemv_gpu import dev, gemv_np, lib
+
 
 KIND = {"group": 0, "row": 1}
 
@@ -42,9 +46,6 @@ def tc_np(x, q, s, kind="group"):
     torch.cuda.synchronize()
     assert rc == 0, lib().af_status_string(rc)
     return y.cpu().numpy().view(np.uint16)
-
-torch = pytest.importorskip("torch")
-pytestmark = pytest.mark.gpu
 
 
 def _faults():

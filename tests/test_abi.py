@@ -76,3 +76,15 @@ def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(ImportError):
         _lib.lib()
+
+
+def test_tp_buffer_holds_partials_and_row_epochs():
+    """The exchange buffer of the fused all-reduce: a 1280-byte header (status,
+    lm_head argmax pairs), partials [2 parity halves][8 source ranks][max_n] as
+    64-bit words, then one 32-bit epoch per row (rounded to 16 bytes) -- the
+    per-row epochs keep every row's tag alternating whatever grid a launch uses."""
+    from atomflow_b200._lib import lib
+    L = lib()
+    for n in (1, 64, 3072, 4097):
+        assert L.af_tp_buffer_bytes(n) == 1280 + 256 + 2 * 8 * n * 8 + ((n * 4 + 15) // 16) * 16
+    assert L.af_tp_buffer_bytes(0) == 0
